@@ -1,0 +1,466 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 probe path (one JSON line on stdout, rank 0).
+
+Headline workload: the sharded HBM copy stream — every GPU copies its own
+fp32[2^30] (4 GiB) buffer, seeded uniform [-1,1), to a second buffer with
+cmb_stream_copy (the reference's kernel_stream_copy, src/mem_global.cu:13-16,
+re-targeted to sm_100a).  One step = one copy of the 4 GiB buffer on every
+GPU; value = algorithmic bytes (read + write) of all GPUs / max-over-ranks
+device time, in GB/s.  Weak scaling: per-GPU work is fixed.
+
+At N=1, rank 0 also runs the other probes of the path once (1 GiB copy and
+sum, 512 MiB chase, TMA tile copy, tcgen05 GEMMs) and reports them under
+"probes"; at N>1 the NVLink peer-store ring and all-to-all are reported there.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the CPU implementation of the same copy (the
+oracle's multi-threaded memcpy, the reference path having no CPU code of its
+own) on a bounded sample, on rank 0 only.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "HBM GB/s & BF16/FP8 TFLOPS per B200 (% of peak); NVLink P2P GB/s at 1/2/4/8 GPU"
+UNIT = "GB/s"
+COPY_ELEMS = 1 << 30  # fp32 per GPU: 4 GiB
+SEED = 0x5EED
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------- ranks
+
+
+class Ranks:
+    """Process-group plumbing: one process per GPU, launched by torchrun."""
+
+    def __init__(self, backend: str):
+        import torch
+        import torch.distributed as dist
+
+        self.torch, self.dist = torch, dist
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
+        if self.world > 1 and not dist.is_initialized():
+            import datetime
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        dev = "cuda" if self.backend == "nccl" else "cpu"
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        dev = "cuda" if self.backend == "nccl" else "cpu"
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1 and self.dist.is_initialized():
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, period_ms: int = 20):
+        self.gpu_index, self.period_ms = gpu_index, period_ms
+        self.proc, self.file, self.t0 = None, None, None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 f"-i", str(self.gpu_index), f"-lms", str(self.period_ms)],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+            self.t0 = time.time()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(2 * self.period_ms / 1000.0)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().splitlines() if r.strip()]
+        self.file.close()
+        os.unlink(self.file.name)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                power.append(float(r[3]))
+            except (ValueError, IndexError):
+                continue
+            for k, name in enumerate(names):
+                if len(r) > 5 + k and r[5 + k].strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------- helpers
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+                "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch recorded from ncu in profiles/<name>.txt, if any
+    (a line `traffic_bytes_per_launch: <int>`)."""
+    path = os.path.join(ROOT, "profiles", name + ".txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+def cpu_memcpy_baseline(sample_bytes: int, steps: int, warmup: int) -> dict:
+    """Times the oracle's multi-threaded memcpy (the CPU implementation of the
+    copy probe) on a bounded sample; GB/s counts read + write bytes."""
+    import numpy as np
+
+    import oracle
+
+    orc = oracle.load()
+    threads = orc.orc_hw_threads()
+    src = np.empty(sample_bytes, np.uint8)
+    dst = np.empty(sample_bytes, np.uint8)
+    orc.orc_fill_bytes(oracle.ptr(src), sample_bytes, SEED)
+    dst.fill(1)  # fault the pages in
+    for _ in range(warmup):
+        orc.orc_memcpy_mt(oracle.ptr(dst), oracle.ptr(src), sample_bytes, threads)
+    total = 0.0
+    for _ in range(steps):
+        total += orc.orc_memcpy_mt(oracle.ptr(dst), oracle.ptr(src), sample_bytes, threads)
+    assert np.array_equal(src[:: 1 << 16], dst[:: 1 << 16])
+    gbs = 2.0 * sample_bytes * steps / total / 1e9
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} x memcpy of {sample_bytes >> 20} MiB (oracle, {threads} threads)",
+            "seconds": round(total, 4)}
+
+
+# ---------------------------------------------------------------- our arm
+
+
+def run_ours(args) -> int:
+    import torch
+
+    import cuda_micro_bench_b200 as cmbpkg
+    from cuda_micro_bench_b200 import check, lib
+
+    ranks = Ranks("nccl")
+    torch.cuda.set_device(ranks.local_rank)
+    dev_index = torch.cuda.current_device()
+    stream = torch.cuda.current_stream()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    n = COPY_ELEMS
+    nbytes = 4 * n
+    src = torch.empty(n, dtype=torch.float32, device="cuda")
+    dst = torch.empty(n, dtype=torch.float32, device="cuda")
+    check("cmb_fill_uniform_f32", ctypes.c_void_p(src.data_ptr()), n,
+          ctypes.c_uint64(SEED + ranks.rank), sh)
+    dst.zero_()
+    torch.cuda.synchronize()
+
+    def step():
+        check("cmb_stream_copy", ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+              nbytes, sh)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # correctness of what is being timed: bit-exact copy
+    ok = bool(torch.equal(src.view(torch.int32), dst.view(torch.int32)))
+    if not ok:
+        raise SystemExit(f"rank {ranks.rank}: copy output differs from input")
+
+    clocks = ClockSampler(dev_index).start()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ranks.barrier()
+    torch.cuda.synchronize()
+    evs[0].record(stream)
+    for k in range(args.steps):
+        step()
+        evs[k + 1].record(stream)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    clk = clocks.stop()
+    launch_ms = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
+    local_ms = evs[0].elapsed_time(evs[-1])
+    total_ms = ranks.max(local_ms)
+    value = ranks.world * 2.0 * nbytes * args.steps / (total_ms * 1e-3) / 1e9
+
+    peaks = measured_peaks()
+    avg_launch_s = statistics.mean(launch_ms) * 1e-3
+    achieved = 2.0 * nbytes / avg_launch_s / 1e9
+    traffic = profile_traffic("stream_copy_4gib")
+    roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": traffic, "peak_source": peaks["source"],
+                "kernel": "k_stream_copy<32,4>", "algorithmic_bytes_per_launch": 2 * nbytes}
+
+    # end to end through the C ABI with pinned host buffers
+    e2e = run_e2e(args, ranks, torch, src, dst, nbytes)
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ranks.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded uniform [-1,1) fp32, SplitMix64)",
+        "config": {"workload": "stream_copy: fp32[2^30] (4 GiB) -> second buffer per GPU, "
+                               "sharded, no exchange",
+                   "bytes_per_gpu_per_step": 2 * nbytes, "parallelism": f"shard{ranks.world}",
+                   "l2": "inputs larger than L2 (4 GiB vs 126 MB)", "impl": "ours"},
+        "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_memcpy_baseline(1 << 30, 8, 1)
+    del src, dst
+    torch.cuda.empty_cache()
+    if not args.no_probes:
+        result["probes"] = run_probes(args, ranks, peaks)
+    if ranks.rank == 0:
+        print(json.dumps(result), flush=True)
+    ranks.close()
+    return 0
+
+
+def run_e2e(args, ranks, torch, dev_a, dev_b, nbytes):
+    """Same metric through cmb_stream_copy_host: pinned host input, H2D, the
+    device copy, D2H of the full result, every step."""
+    from cuda_micro_bench_b200 import check
+
+    host_src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host_dst = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host_src.copy_(dev_a.view(torch.uint8).cpu())
+    chunk = 64 << 20
+    steps = max(1, min(args.e2e_steps, args.steps))
+
+    def e2e_step():
+        check("cmb_stream_copy_host", ctypes.c_void_p(host_dst.data_ptr()),
+              ctypes.c_void_p(host_src.data_ptr()), nbytes, ctypes.c_void_p(dev_a.data_ptr()),
+              ctypes.c_void_p(dev_b.data_ptr()), nbytes, chunk)
+
+    e2e_step()
+    if not torch.equal(host_src[:: 1 << 12], host_dst[:: 1 << 12]):
+        raise SystemExit("e2e copy output differs from input")
+    ranks.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        e2e_step()
+    local = time.perf_counter() - t0
+    ranks.barrier()
+    total = ranks.max(local)
+    value = ranks.world * 2.0 * nbytes * steps / total / 1e9
+    del host_src, host_dst
+    return {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": nbytes,
+            "d2h_bytes_per_step": nbytes, "steps": steps,
+            "path": "cmb_stream_copy_host (pinned host -> device copy -> host, 64 MiB chunks)"}
+
+
+# ---------------------------------------------------------------- probes
+
+
+def _time_launches(torch, stream, fn, reps):
+    """Per-launch device times (ms) of `reps` back-to-back calls of fn."""
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    torch.cuda.synchronize()
+    evs[0].record(stream)
+    for k in range(reps):
+        fn()
+        evs[k + 1].record(stream)
+    torch.cuda.synchronize()
+    return [evs[k].elapsed_time(evs[k + 1]) for k in range(reps)]
+
+
+def probe_stream_1gib(torch, stream, sh, peaks):
+    """Config: fp32[2^28] (1 GiB) copy (bit-exact) and sum (checked against
+    an fp64 sum, rel 1e-5); median of 5 timed launches after one warm-up, as
+    the reference's measure() (src/mem_global.cu:42-53)."""
+    from cuda_micro_bench_b200 import check, lib
+
+    n = 1 << 28
+    src = torch.empty(n, dtype=torch.float32, device="cuda")
+    dst = torch.empty(n, dtype=torch.float32, device="cuda")
+    check("cmb_fill_uniform_f32", ctypes.c_void_p(src.data_ptr()), n, ctypes.c_uint64(SEED), sh)
+    ws_bytes = lib.cmb_stream_sum_workspace_bytes(n)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty(1, dtype=torch.float64, device="cuda")
+    copy = lambda: check("cmb_stream_copy", ctypes.c_void_p(dst.data_ptr()),
+                         ctypes.c_void_p(src.data_ptr()), 4 * n, sh)
+    ssum = lambda: check("cmb_stream_sum_f32", ctypes.c_void_p(src.data_ptr()), n,
+                         ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                         ws_bytes, sh)
+    copy_ms = statistics.median(_time_launches(torch, stream, copy, 6)[1:])
+    sum_ms = statistics.median(_time_launches(torch, stream, ssum, 6)[1:])
+    copy_ok = bool(torch.equal(src.view(torch.int32), dst.view(torch.int32)))
+    ref = float(src.double().sum().item())  # fp64 check sum
+    got = float(out.item())
+    rel = abs(got - ref) / abs(ref)
+    copy_gbs = 2.0 * 4 * n / (copy_ms * 1e-3) / 1e9
+    read_gbs = 4.0 * n / (sum_ms * 1e-3) / 1e9
+    del src, dst, ws, out
+    return {
+        "copy_1gib": {"GB/s": round(copy_gbs, 2), "frac_of_measured_hbm": round(copy_gbs / peaks["hbm_gbs"], 4),
+                      "frac_of_8tbs_spec": round(copy_gbs / 8000.0, 4), "bit_exact": copy_ok,
+                      "ms": round(copy_ms, 4)},
+        "sum_1gib": {"GB/s": round(read_gbs, 2), "frac_of_measured_hbm": round(read_gbs / peaks["hbm_gbs"], 4),
+                     "frac_of_8tbs_spec": round(read_gbs / 8000.0, 4), "sum": got, "fp64_sum": ref,
+                     "rel_err": rel, "within_1e-5": rel <= 1e-5, "ms": round(sum_ms, 4)},
+    }
+
+
+def probe_chase(torch, stream, sh, hops):
+    """Config: 512 MiB link array, Sattolo cycle from a seed, dependent
+    .cg loads; final index vs the host walk (the reference's self-check,
+    include/memory_chase.h:152-164)."""
+    import numpy as np
+
+    from cuda_micro_bench_b200 import check
+
+    nbytes = 512 << 20
+    links = np.empty(nbytes // 4, np.uint32)
+    check("cmb_chase_build_links", ctypes.c_void_p(links.ctypes.data), nbytes,
+          ctypes.c_uint64(0xC0DA))
+    d = torch.from_numpy(links.view(np.int32)).cuda()
+    out = torch.zeros(4, dtype=torch.int64, device="cuda")
+    warm = 1024
+    check("cmb_chase_run", ctypes.c_void_p(d.data_ptr()), links.size, ctypes.c_uint64(warm),
+          ctypes.c_uint64(hops), 1, ctypes.c_void_p(out.data_ptr()), sh)
+    torch.cuda.synchronize()
+    cycles, idx, ns, status = [int(v) for v in out.cpu().numpy().view(np.uint64)]
+    expect = ctypes.c_uint32(0)
+    check("cmb_chase_host_walk", ctypes.c_void_p(links.ctypes.data), links.size,
+          ctypes.c_uint64(warm + hops), ctypes.byref(expect))
+    expect = expect.value
+    del d
+    return {"working_set_bytes": nbytes, "hops": hops, "ns_per_hop": round(ns / hops, 3),
+            "cycles_per_hop": round(cycles / hops, 3), "status": status,
+            "endpoint_matches_host_walk": idx == expect}
+
+
+def run_probes(args, ranks, peaks) -> dict:
+    import torch
+
+    stream = torch.cuda.current_stream()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    out = {}
+    if ranks.world == 1:
+        out.update(probe_stream_1gib(torch, stream, sh, peaks))
+        out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (24 if args.full_chase else 22))
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------- reference arm
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    base = cpu_memcpy_baseline(1 << 30, args.steps_ref, max(1, min(args.warmup, 3)))
+    result = {
+        "metric": METRIC, "value": base["value"], "unit": UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps_ref,
+        "warmup": max(1, min(args.warmup, 3)), "ms_per_step": round(1e3 * base["seconds"] / args.steps_ref, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded bytes, SplitMix64)",
+        "config": {"workload": "stream_copy on host cores: memcpy sample of the 4 GiB copy",
+                   "parallelism": "host threads", "impl": "reference"},
+        "impl": "reference", "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--steps-ref", type=int, default=8)
+    ap.add_argument("--no-probes", action="store_true", help="headline only")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--full-chase", action="store_true", help="2^24 chase hops (default 2^22)")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus != world:
+        ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,68 @@
+"""ctypes binding of the C ABI in include/cmb_b200.h.
+
+Loading fails loudly (ImportError) when ``lib/libcmb_b200.so`` has not been
+built: the probes have no other implementation.
+"""
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+library_path = os.path.join(HERE, "lib", "libcmb_b200.so")
+
+if not os.path.exists(library_path):
+    raise ImportError(
+        f"{library_path} is missing: build it with `python -m cuda_micro_bench_b200.build` "
+        "(the probe path has no CPU fallback)"
+    )
+
+lib = ctypes.CDLL(library_path)
+
+_i, _u32, _u64, _sz = ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t
+_p, _f, _d, _s = ctypes.c_void_p, ctypes.c_float, ctypes.c_double, ctypes.c_char_p
+
+# name -> (restype, argtypes); the stream argument is a raw handle (c_void_p).
+SIGNATURES = {
+    "cmb_status_string": (_s, [_i]),
+    "cmb_last_error": (_s, []),
+    "cmb_version": (_s, []),
+    "cmb_fill_hash_u32": (_i, [_p, _sz, _p]),
+    "cmb_fill_uniform_f32": (_i, [_p, _sz, _u64, _p]),
+    "cmb_fill_bytes": (_i, [_p, _sz, _u64, _p]),
+    "cmb_fill_normal_bf16": (_i, [_p, _sz, _u64, _f, _p]),
+    "cmb_stream_copy": (_i, [_p, _p, _sz, _p]),
+    "cmb_stream_copy_tuned": (_i, [_p, _p, _sz, _i, _i, _i, _p]),
+    "cmb_stream_sum_workspace_bytes": (_sz, [_sz]),
+    "cmb_stream_sum_f32": (_i, [_p, _sz, _p, _p, _sz, _p]),
+    "cmb_stream_copy_host": (_i, [_p, _p, _sz, _p, _p, _sz, _sz]),
+    "cmb_chase_build_links": (_i, [_p, _sz, _u64]),
+    "cmb_chase_run": (_i, [_p, _sz, _u64, _u64, _i, _p, _p]),
+    "cmb_chase_host_walk": (_i, [_p, _sz, _u64, _p]),
+    "cmb_results_set_device": (_i, [_s, _s, _i, _i, _i, _i]),
+    "cmb_results_log": (_i, [_s, _s, _d, _s]),
+    "cmb_results_write_json": (_i, [_s]),
+    "cmb_results_clear": (_i, []),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class CmbError(RuntimeError):
+    """A cmb_* call returned a non-zero cmb_status."""
+
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        name = lib.cmb_status_string(status).decode()
+        detail = lib.cmb_last_error().decode()
+        super().__init__(f"{fn} -> {name}: {detail}")
+
+
+def check(fn: str, *args) -> int:
+    """Calls lib.<fn>(*args) and raises CmbError on a non-zero status."""
+    rc = getattr(lib, fn)(*args)
+    if rc != 0:
+        raise CmbError(fn, rc)
+    return rc

@@ -1,0 +1,34 @@
+// cmb_host.h — host-side error handling shared by the C ABI entry points.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+
+#include "../../include/cmb_b200.h"
+
+namespace cmb {
+
+// Records a one-line reason for the calling thread and returns `code`.
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+// Clears the calling thread's last error.
+void clear_error();
+
+// Number of SMs of the current device (cached per device).
+int current_sm_count();
+// Compute capability major*10+minor of the current device.
+int current_cc();
+
+}  // namespace cmb
+
+#define CMB_CUDA_TRY(call)                                                              \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return ::cmb::fail(CMB_ERR_CUDA, "%s:%d: %s: %s", __FILE__, __LINE__, #call,      \
+                         cudaGetErrorString(e_));                                       \
+  } while (0)
+
+// Checks the launch that was just enqueued.
+#define CMB_LAUNCH_CHECK() CMB_CUDA_TRY(cudaGetLastError())

@@ -1,0 +1,143 @@
+/*
+ * cmb_b200.h — C ABI of the B200 (sm_100a) probe library libcmb_b200.so.
+ *
+ * The reference suite (cuda_micro_bench) has no FFI: its probe path is a set
+ * of C++ functions `void cmb::benchmark_<section>()` that allocate, launch,
+ * time and log inside one executable.  This header exposes the same path as
+ * plain C entry points so any host (C, C++, Python ctypes, cgo, JNI) can
+ * bind it: the kernels take device pointers and sizes and launch on the
+ * caller's stream; the section entry points run a whole probe section and
+ * log into the results table that cmb_results_write_json() writes in the
+ * reference's results.json schema.
+ *
+ * Conventions
+ *   - Every function returns a cmb_status (0 = CMB_OK).  On failure a
+ *     one-line reason is available from cmb_last_error() (per thread).
+ *   - Device pointers are plain pointers to device memory of the current
+ *     device; host pointers say so in their name.
+ *   - `stream` is a CUDA stream handle (cudaStream_t / CUstream); NULL is
+ *     the legacy default stream.  Launch functions are asynchronous.
+ *   - Kernels whose work is bounded by a device-side wait write a status
+ *     word (cmb_status) to `status` (device int*, may be NULL) instead of
+ *     hanging: CMB_ERR_TIMEOUT means a wait gave up.
+ */
+#ifndef CMB_B200_H
+#define CMB_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *cmb_stream_t;
+
+typedef enum {
+  CMB_OK = 0,
+  CMB_ERR_INVALID_ARG = 1,  /* bad size, alignment or pointer */
+  CMB_ERR_CUDA = 2,         /* a CUDA runtime/driver call failed */
+  CMB_ERR_TIMEOUT = 3,      /* a bounded device-side wait expired */
+  CMB_ERR_UNSUPPORTED = 4,  /* device is not sm_100 or lacks a feature */
+  CMB_ERR_MISMATCH = 5,     /* a probe's self-check failed */
+  CMB_ERR_IO = 6            /* results file could not be written */
+} cmb_status;
+
+/* --- status -------------------------------------------------------- */
+
+/* Name of a status code ("CMB_OK", ...). */
+const char *cmb_status_string(int status);
+/* Reason for the last failure on the calling thread ("" if none). */
+const char *cmb_last_error(void);
+/* Library version string. */
+const char *cmb_version(void);
+
+/* --- seeded input generators (not part of any timed region) ---------- */
+
+/* dst[i] = fmix32(i + 0x9e3779b9): replaces kernel_init_stream
+ * (src/mem_global.cu:5-12). */
+int cmb_fill_hash_u32(uint32_t *dst, size_t n, cmb_stream_t stream);
+/* dst[i] = uniform fp32 in [-1,1) from SplitMix64(seed) output i. */
+int cmb_fill_uniform_f32(float *dst, size_t n, uint64_t seed, cmb_stream_t stream);
+/* dst[i] = byte i%8 of SplitMix64(seed) output i/8. */
+int cmb_fill_bytes(uint8_t *dst, size_t n, uint64_t seed, cmb_stream_t stream);
+/* dst[i] = bf16(scale * N(0,1)), Box-Muller on SplitMix64(seed). */
+int cmb_fill_normal_bf16(uint16_t *dst, size_t n, uint64_t seed, float scale,
+                         cmb_stream_t stream);
+
+/* --- global-memory streams (src/mem_global.cu) ----------------------- */
+
+/* dst[0:bytes) = src[0:bytes).  Replaces kernel_stream_copy and its launch
+ * (src/mem_global.cu:13-16,46).  Any size and alignment; 16-byte aligned
+ * pointers take the vector path. */
+int cmb_stream_copy(void *dst, const void *src, size_t bytes, cmb_stream_t stream);
+/* cmb_stream_copy with an explicit launch shape, for sweeps: vec_bytes 16 or
+ * 32, unroll 1/2/4/8 vectors in flight per thread, ctas_per_sm 1..8 CTAs of
+ * 256 threads per SM. */
+int cmb_stream_copy_tuned(void *dst, const void *src, size_t bytes, int vec_bytes, int unroll,
+                          int ctas_per_sm, cmb_stream_t stream);
+
+/* Workspace bytes cmb_stream_sum_f32 needs for n values. */
+size_t cmb_stream_sum_workspace_bytes(size_t n);
+/* *out_sum (device double) = sum of src[0:n) (fp32 loads, fp32 per-thread
+ * partials, fp64 block and grid combine, fixed order).  Replaces the
+ * read-only stream kernel_stream_read (src/mem_global.cu:17-26,47), whose
+ * XOR sink is replaced by a checkable sum.  `workspace` is device memory of
+ * cmb_stream_sum_workspace_bytes(n) bytes; it needs no initialisation. */
+int cmb_stream_sum_f32(const float *src, size_t n, double *out_sum, void *workspace,
+                       size_t workspace_bytes, cmb_stream_t stream);
+
+/* Host-buffer stream copy: host_dst = host_src through the device.  Copies
+ * chunks host->device, runs cmb_stream_copy on each, copies them back, with
+ * the three steps of consecutive chunks overlapped on three streams.
+ * dev_a/dev_b are device staging buffers of dev_bytes each (dev_bytes >=
+ * 2*chunk); host buffers should be pinned for full speed.  Blocks until
+ * host_dst is complete. */
+int cmb_stream_copy_host(void *host_dst, const void *host_src, size_t bytes, void *dev_a,
+                         void *dev_b, size_t dev_bytes, size_t chunk);
+
+/* --- dependent-load pointer chase (src/memory_chase.cu,
+ *     include/memory_chase.h) ------------------------------------------ */
+
+/* Host: fill host_links (bytes/4 words) with one Sattolo cycle over the
+ * bytes/128 slots of 128 B (word 0 of each slot links to the next slot's
+ * word index; the other words hold fmix32 of their index).  Replaces the
+ * host cycle build of measureRandomChase (include/memory_chase.h:125-138). */
+int cmb_chase_build_links(uint32_t *host_links, size_t bytes, uint64_t seed);
+
+/* One thread follows idx = links[idx] from word 0: `warmup` untimed hops,
+ * then `hops` timed hops.  bypass_l1 = 1 uses ld.global.cg, 0 uses
+ * ld.global.ca.  out (device, 4 x uint64) = {SM cycles of the timed hops,
+ * final index, globaltimer ns of the timed hops, status}; status is
+ * CMB_ERR_INVALID_ARG (and the walk is skipped) if a slot head of the
+ * `words`-word array is not an in-range slot index.  Replaces
+ * kernel_random_chase_cg/_ca (src/memory_chase.cu:6-34). */
+int cmb_chase_run(const uint32_t *links, size_t words, uint64_t warmup, uint64_t hops,
+                  int bypass_l1, uint64_t *out, cmb_stream_t stream);
+
+/* Host: *out_index = the index reached after `hops` hops of idx =
+ * host_links[idx] from 0, the expected endpoint of cmb_chase_run with
+ * warmup + hops = `hops` (the reference's self-check,
+ * include/memory_chase.h:152-153,161-164).  CMB_ERR_INVALID_ARG if the walk
+ * leaves the array. */
+int cmb_chase_host_walk(const uint32_t *host_links, size_t words, uint64_t hops,
+                        uint32_t *out_index);
+
+/* --- results table (include/result_logger.h, src/result_logger.cu) --- */
+
+/* Same meaning as ResultLogger::setDevice (include/result_logger.h:113-121). */
+int cmb_results_set_device(const char *name, const char *arch, int sm_count, int clock_khz,
+                           int mem_clock_khz, int mem_bus_width);
+/* Same meaning as ResultLogger::log (include/result_logger.h:123-126); unit
+ * "N/A" writes a null value. */
+int cmb_results_log(const char *section, const char *key, double value, const char *unit);
+/* Writes the table in the reference's results.json format
+ * (src/result_logger.cu:10-43). */
+int cmb_results_write_json(const char *path);
+/* Empties the table and the device fields. */
+int cmb_results_clear(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CMB_B200_H */

@@ -1,0 +1,364 @@
+/*
+ * oracle.c — CPU oracle for the probe path (TEST INFRASTRUCTURE ONLY; see
+ * oracle.h).  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline load this file's library.
+ */
+#define _GNU_SOURCE
+#include "oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+/* ------------------------------------------------------------------ */
+/* generators                                                          */
+/* ------------------------------------------------------------------ */
+
+static const uint64_t kGolden = 0x9E3779B97F4A7C15ULL;
+
+static inline uint64_t mix64(uint64_t z) {
+  /* SplitMix64 output function (Steele, Lea, Flood 2014). */
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+uint64_t orc_splitmix64_at(uint64_t seed, uint64_t i) {
+  return mix64(seed + (i + 1) * kGolden);
+}
+
+uint32_t orc_hash32(uint32_t i) {
+  /* src/mem_global.cu:7-10 */
+  uint32_t x = i + 0x9e3779b9U;
+  x = (x ^ (x >> 16)) * 0x85ebca6bU;
+  x = (x ^ (x >> 13)) * 0xc2b2ae35U;
+  return x ^ (x >> 16);
+}
+
+void orc_fill_hash_u32(uint32_t *out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = orc_hash32((uint32_t)i);
+}
+
+void orc_fill_uniform_f32(float *out, size_t n, uint64_t seed) {
+  for (size_t i = 0; i < n; ++i) {
+    uint32_t u = (uint32_t)(orc_splitmix64_at(seed, i) >> 40);
+    out[i] = (float)u * 0x1p-23f - 1.0f;
+  }
+}
+
+void orc_fill_bytes(uint8_t *out, size_t n, uint64_t seed) {
+  for (size_t i = 0; i < n; ++i) {
+    uint64_t w = orc_splitmix64_at(seed, i >> 3);
+    out[i] = (uint8_t)(w >> (8 * (i & 7)));
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* pointer chase                                                       */
+/* ------------------------------------------------------------------ */
+
+void orc_chase_build(uint32_t *links, size_t bytes, uint64_t seed) {
+  const size_t words = bytes / 4, slots = bytes / 128;
+  for (size_t w = 0; w < words; ++w) links[w] = orc_hash32((uint32_t)w);
+  if (slots == 0) return;
+  uint32_t *perm = (uint32_t *)malloc(slots * sizeof(uint32_t));
+  for (size_t s = 0; s < slots; ++s) perm[s] = (uint32_t)s;
+  /* Sattolo: for i = n-1 .. 1, swap perm[i] with perm[j], j uniform in
+   * [0, i).  Draw k of the SplitMix64 stream picks j for step k. */
+  uint64_t k = 0;
+  for (size_t i = slots - 1; i >= 1; --i, ++k) {
+    uint64_t r = orc_splitmix64_at(seed, k);
+    size_t j = (size_t)(((unsigned __int128)r * (uint64_t)i) >> 64);
+    uint32_t t = perm[i];
+    perm[i] = perm[j];
+    perm[j] = t;
+  }
+  /* perm is one n-cycle; slot s links to slot perm[s]. */
+  for (size_t s = 0; s < slots; ++s) links[s * 32] = perm[s] * 32u;
+  free(perm);
+}
+
+uint32_t orc_chase_walk(const uint32_t *links, uint64_t hops, uint32_t start) {
+  uint32_t idx = start;
+  for (uint64_t h = 0; h < hops; ++h) idx = links[idx];
+  return idx;
+}
+
+int orc_chase_is_single_cycle(const uint32_t *links, size_t bytes) {
+  const size_t slots = bytes / 128;
+  if (slots == 0) return 0;
+  uint8_t *seen = (uint8_t *)calloc(slots, 1);
+  uint32_t idx = 0;
+  size_t count = 0;
+  int ok = 1;
+  do {
+    if (idx % 32 != 0 || idx / 32 >= slots || seen[idx / 32]) { ok = 0; break; }
+    seen[idx / 32] = 1;
+    ++count;
+    idx = links[idx];
+  } while (idx != 0);
+  free(seen);
+  return ok && count == slots;
+}
+
+/* ------------------------------------------------------------------ */
+/* threaded sum / memcpy                                               */
+/* ------------------------------------------------------------------ */
+
+int orc_hw_threads(void) {
+  long n = sysconf(_SC_NPROCESSORS_ONLN);
+  return n > 0 ? (int)n : 1;
+}
+
+static int pick_threads(int threads) {
+  int t = threads > 0 ? threads : orc_hw_threads();
+  return t > 256 ? 256 : t;
+}
+
+typedef struct {
+  const float *x;
+  size_t begin, end;
+  double out;
+} sum_job;
+
+static void *sum_worker(void *p) {
+  sum_job *j = (sum_job *)p;
+  /* Blocks of 4096 values summed in fp64, then the block sums in fp64. */
+  double acc = 0.0;
+  for (size_t b = j->begin; b < j->end; b += 4096) {
+    size_t e = b + 4096 < j->end ? b + 4096 : j->end;
+    double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    size_t i = b;
+    for (; i + 4 <= e; i += 4) {
+      s0 += j->x[i];
+      s1 += j->x[i + 1];
+      s2 += j->x[i + 2];
+      s3 += j->x[i + 3];
+    }
+    for (; i < e; ++i) s0 += j->x[i];
+    acc += (s0 + s1) + (s2 + s3);
+  }
+  j->out = acc;
+  return NULL;
+}
+
+double orc_sum_f64(const float *x, size_t n, int threads) {
+  int t = pick_threads(threads);
+  if ((size_t)t > n / 4096 + 1) t = (int)(n / 4096 + 1);
+  pthread_t th[256];
+  sum_job jobs[256];
+  size_t per = (n + t - 1) / t;
+  for (int k = 0; k < t; ++k) {
+    jobs[k].x = x;
+    jobs[k].begin = (size_t)k * per < n ? (size_t)k * per : n;
+    jobs[k].end = (size_t)(k + 1) * per < n ? (size_t)(k + 1) * per : n;
+    pthread_create(&th[k], NULL, sum_worker, &jobs[k]);
+  }
+  double total = 0.0;
+  for (int k = 0; k < t; ++k) {
+    pthread_join(th[k], NULL);
+    total += jobs[k].out;
+  }
+  return total;
+}
+
+typedef struct {
+  char *dst;
+  const char *src;
+  size_t n;
+} copy_job;
+
+static void *copy_worker(void *p) {
+  copy_job *j = (copy_job *)p;
+  memcpy(j->dst, j->src, j->n);
+  return NULL;
+}
+
+double orc_memcpy_mt(void *dst, const void *src, size_t n, int threads) {
+  int t = pick_threads(threads);
+  pthread_t th[256];
+  copy_job jobs[256];
+  size_t per = ((n + t - 1) / t + 63) & ~(size_t)63;
+  struct timespec a, b;
+  clock_gettime(CLOCK_MONOTONIC, &a);
+  int used = 0;
+  for (int k = 0; k < t; ++k) {
+    size_t off = (size_t)k * per;
+    if (off >= n) break;
+    jobs[k].dst = (char *)dst + off;
+    jobs[k].src = (const char *)src + off;
+    jobs[k].n = off + per <= n ? per : n - off;
+    pthread_create(&th[k], NULL, copy_worker, &jobs[k]);
+    ++used;
+  }
+  for (int k = 0; k < used; ++k) pthread_join(th[k], NULL);
+  clock_gettime(CLOCK_MONOTONIC, &b);
+  return (double)(b.tv_sec - a.tv_sec) + 1e-9 * (double)(b.tv_nsec - a.tv_nsec);
+}
+
+/* ------------------------------------------------------------------ */
+/* number formats                                                      */
+/* ------------------------------------------------------------------ */
+
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+float orc_bf16_to_f32(uint16_t v) { return u2f((uint32_t)v << 16); }
+
+uint16_t orc_f32_to_bf16_rne(float f) {
+  uint32_t u = f2u(f);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu))
+    return (uint16_t)((u >> 16) | 0x0040u); /* quiet NaN */
+  uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7fffu + lsb;
+  return (uint16_t)(u >> 16);
+}
+
+/* OCP 8-bit floating point, E4M3: bias 7, no infinities, S.1111.111 = NaN,
+ * largest finite 448, smallest subnormal 2^-9. */
+float orc_e4m3_to_f32(uint8_t v) {
+  int s = v >> 7, e = (v >> 3) & 0xf, m = v & 7;
+  float mag;
+  if (e == 0xf && m == 7) return NAN;
+  if (e == 0) mag = ldexpf((float)m, -9);
+  else mag = ldexpf((float)(8 + m), e - 10);
+  return s ? -mag : mag;
+}
+
+uint8_t orc_f32_to_e4m3_satfinite(float f) {
+  uint8_t sign = (f2u(f) >> 31) ? 0x80 : 0x00;
+  if (isnan(f)) return 0x7f;
+  float a = fabsf(f);
+  if (a >= 448.0f) return sign | 0x7e; /* saturate (inf included) */
+  /* Candidates are the 127 finite non-negative codes; pick the nearest,
+   * ties to the even code (even mantissa LSB). */
+  /* Quantum in the binade of a: normal e in [1,15] covers [2^-6, 2^9). */
+  double x = (double)a;
+  int code;
+  if (x < 0x1p-6) {
+    /* subnormal grid: multiples of 2^-9, codes 0..7 (8 = 2^-6 normal) */
+    double q = x * 512.0; /* exact */
+    double r = nearbyint(q); /* default rounding mode: ties to even */
+    code = (int)r; /* 0..8; 8 is the smallest normal (e=1, m=0) */
+  } else {
+    int e;
+    frexp(x, &e); /* x = f * 2^e, f in [0.5, 1) */
+    int ub = e - 1; /* unbiased exponent, x in [2^ub, 2^(ub+1)) */
+    double q = ldexp(x, 3 - ub); /* in [8, 16) */
+    double r = nearbyint(q);
+    int m = (int)r - 8; /* 0..8; 8 means carry into the next binade */
+    int be = ub + 7;
+    if (m == 8) { m = 0; be += 1; }
+    code = (be << 3) | m;
+    if (code > 0x7e) code = 0x7e;
+  }
+  return sign | (uint8_t)code;
+}
+
+float orc_amax_bf16(const uint16_t *x, size_t n) {
+  float m = 0.0f;
+  for (size_t i = 0; i < n; ++i) {
+    float a = fabsf(orc_bf16_to_f32(x[i]));
+    if (a > m) m = a;
+  }
+  return m;
+}
+
+void orc_quantize_e4m3(const uint16_t *x, size_t n, float inv_scale, uint8_t *q) {
+  for (size_t i = 0; i < n; ++i) {
+    float v = orc_bf16_to_f32(x[i]) * inv_scale; /* one fp32 RN multiply */
+    q[i] = orc_f32_to_e4m3_satfinite(v);
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* GEMM                                                                */
+/* ------------------------------------------------------------------ */
+
+void orc_gemm_tile_f64(const void *A, const void *B, int dtype, int K, int lda,
+                       int ldb, int row0, int col0, int tm, int tn,
+                       double scale_a, double scale_b, double *out) {
+  double *arow = (double *)malloc((size_t)K * sizeof(double));
+  double *bt = (double *)malloc((size_t)tn * K * sizeof(double));
+  for (int j = 0; j < tn; ++j)
+    for (int k = 0; k < K; ++k) {
+      size_t o = (size_t)(col0 + j) * ldb + k;
+      bt[(size_t)j * K + k] =
+          dtype == 0 ? (double)orc_bf16_to_f32(((const uint16_t *)B)[o])
+                     : (double)orc_e4m3_to_f32(((const uint8_t *)B)[o]) * scale_b;
+    }
+  for (int i = 0; i < tm; ++i) {
+    for (int k = 0; k < K; ++k) {
+      size_t o = (size_t)(row0 + i) * lda + k;
+      arow[k] = dtype == 0 ? (double)orc_bf16_to_f32(((const uint16_t *)A)[o])
+                           : (double)orc_e4m3_to_f32(((const uint8_t *)A)[o]) * scale_a;
+    }
+    for (int j = 0; j < tn; ++j) {
+      const double *b = bt + (size_t)j * K;
+      double s = 0.0;
+      for (int k = 0; k < K; ++k) s += arow[k] * b[k];
+      out[(size_t)i * tn + j] = s;
+    }
+  }
+  free(arow);
+  free(bt);
+}
+
+typedef struct {
+  const uint16_t *A, *B;
+  float *C;
+  int N, K, r0, r1;
+} gemm_job;
+
+static void *gemm_worker(void *p) {
+  gemm_job *g = (gemm_job *)p;
+  const int KB = 256;
+  float *a = (float *)malloc(sizeof(float) * KB);
+  float *b = (float *)malloc(sizeof(float) * KB * 64);
+  for (int r = g->r0; r < g->r1; ++r)
+    for (int c = 0; c < g->N; ++c) g->C[(size_t)r * g->N + c] = 0.0f;
+  for (int k0 = 0; k0 < g->K; k0 += KB) {
+    int kb = g->K - k0 < KB ? g->K - k0 : KB;
+    for (int c0 = 0; c0 < g->N; c0 += 64) {
+      int cb = g->N - c0 < 64 ? g->N - c0 : 64;
+      for (int c = 0; c < cb; ++c)
+        for (int k = 0; k < kb; ++k)
+          b[c * KB + k] = orc_bf16_to_f32(g->B[(size_t)(c0 + c) * g->K + k0 + k]);
+      for (int r = g->r0; r < g->r1; ++r) {
+        for (int k = 0; k < kb; ++k) a[k] = orc_bf16_to_f32(g->A[(size_t)r * g->K + k0 + k]);
+        float *crow = g->C + (size_t)r * g->N + c0;
+        for (int c = 0; c < cb; ++c) {
+          const float *bc = b + c * KB;
+          float s = 0.0f;
+          for (int k = 0; k < kb; ++k) s += a[k] * bc[k];
+          crow[c] += s;
+        }
+      }
+    }
+  }
+  free(a);
+  free(b);
+  return NULL;
+}
+
+void orc_gemm_bf16_rows_f32(const uint16_t *A, const uint16_t *B, float *C,
+                            int N, int K, int row0, int rows, int threads) {
+  int t = pick_threads(threads);
+  if (t > rows) t = rows > 0 ? rows : 1;
+  pthread_t th[256];
+  gemm_job jobs[256];
+  int per = (rows + t - 1) / t;
+  int used = 0;
+  for (int k = 0; k < t; ++k) {
+    int a = row0 + k * per, b = row0 + (k + 1) * per;
+    if (a >= row0 + rows) break;
+    if (b > row0 + rows) b = row0 + rows;
+    jobs[k] = (gemm_job){A, B, C, N, K, a, b};
+    pthread_create(&th[k], NULL, gemm_worker, &jobs[k]);
+    ++used;
+  }
+  for (int k = 0; k < used; ++k) pthread_join(th[k], NULL);
+}
