@@ -34,7 +34,6 @@ sys.path.insert(0, ROOT)
 
 METRIC = "HBM GB/s & BF16/FP8 TFLOPS per B200 (% of peak); NVLink P2P GB/s at 1/2/4/8 GPU"
 UNIT = "GB/s"
-COPY_ELEMS = 1 << 30  # fp32 per GPU: 4 GiB
 SEED = 0x5EED
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
@@ -216,7 +215,7 @@ def run_ours(args) -> int:
     dev_index = torch.cuda.current_device()
     stream = torch.cuda.current_stream()
     sh = ctypes.c_void_p(stream.cuda_stream)
-    n = COPY_ELEMS
+    n = int(args.gib * (1 << 28))
     nbytes = 4 * n
     src = torch.empty(n, dtype=torch.float32, device="cuda")
     dst = torch.empty(n, dtype=torch.float32, device="cuda")
@@ -260,18 +259,18 @@ def run_ours(args) -> int:
     roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "traffic": traffic, "peak_source": peaks["source"],
-                "kernel": "k_stream_copy<32,4>", "algorithmic_bytes_per_launch": 2 * nbytes}
+                "kernel": "k_stream_copy<32,2>", "algorithmic_bytes_per_launch": 2 * nbytes}
 
     # end to end through the C ABI with pinned host buffers
-    e2e = run_e2e(args, ranks, torch, src, dst, nbytes)
+    e2e = run_e2e(args, ranks, torch, src, dst, nbytes) if args.e2e_steps > 0 else None
 
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ranks.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded uniform [-1,1) fp32, SplitMix64)",
-        "config": {"workload": "stream_copy: fp32[2^30] (4 GiB) -> second buffer per GPU, "
-                               "sharded, no exchange",
+        "config": {"workload": f"stream_copy: fp32[{n}] ({nbytes / 2**30:g} GiB) -> second "
+                               "buffer per GPU, sharded, no exchange",
                    "bytes_per_gpu_per_step": 2 * nbytes, "parallelism": f"shard{ranks.world}",
                    "l2": "inputs larger than L2 (4 GiB vs 126 MB)", "impl": "ours"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps,
@@ -446,7 +445,8 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=3, help="0 skips the e2e leg")
+    ap.add_argument("--gib", type=float, default=4.0, help="copy size per GPU in GiB (default 4)")
     ap.add_argument("--steps-ref", type=int, default=8)
     ap.add_argument("--no-probes", action="store_true", help="headline only")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -189,7 +189,7 @@ __device__ __forceinline__ void report_status(int *status, int code) {
 // cluster-wide destination form is used anywhere in this library)
 
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
-  asm volatile("prefetch.tensor.global.tile [%0];" ::"l"(tmap) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_1d(uint32_t dst, const void *tmap, int32_t x,

@@ -6,11 +6,11 @@
 // contiguous 32 * VB byte span, loads use the non-coherent path without L1
 // allocation and stores are evict-first, so nothing of the stream is kept.
 //
-// Sum: the same loop with fp32 accumulators (UNROLL * VB / 4 independent
-// partial sums per thread), combined per thread and per CTA in fp64; each
-// CTA writes one fp64 partial to the workspace, and the last CTA to finish
-// (atomic ticket) adds the partials in CTA order, so the result does not
-// depend on CTA scheduling.
+// Sum: the same loop; each loaded vector is summed pairwise in fp32 and
+// added to one of UNROLL fp64 accumulators per thread, which are combined
+// per CTA in fp64; each CTA writes one fp64 partial to the workspace, and
+// the last CTA to finish (atomic ticket) adds the partials in CTA order, so
+// the result does not depend on CTA scheduling.
 #include "cmb_device.cuh"
 #include "cmb_host.h"
 
@@ -35,6 +35,10 @@ struct Vec<16> {
                  "r"(w[2]), "r"(w[3])
                  : "memory");
   }
+  __device__ __forceinline__ float pairwise_sum() const {
+    return (__uint_as_float(w[0]) + __uint_as_float(w[1])) +
+           (__uint_as_float(w[2]) + __uint_as_float(w[3]));
+  }
 };
 
 template <>
@@ -50,6 +54,12 @@ struct Vec<32> {
     asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]),
                  "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
                  : "memory");
+  }
+  __device__ __forceinline__ float pairwise_sum() const {
+    return ((__uint_as_float(w[0]) + __uint_as_float(w[1])) +
+            (__uint_as_float(w[2]) + __uint_as_float(w[3]))) +
+           ((__uint_as_float(w[4]) + __uint_as_float(w[5])) +
+            (__uint_as_float(w[6]) + __uint_as_float(w[7])));
   }
 };
 
@@ -121,11 +131,11 @@ __global__ void __launch_bounds__(kStreamThreads) k_stream_sum(const float *__re
   constexpr int F = VB / 4;  // floats per vector
   const float *body = src + head;
   const size_t nvec = (n - head) / F;
-  float acc[UNROLL][F];
+  // Each vector's F floats are added pairwise in fp32 (error of a few ulp of
+  // a value of order sqrt(F)); the vector sums accumulate in fp64.
+  double acc[UNROLL];
 #pragma unroll
-  for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-    for (int f = 0; f < F; ++f) acc[u][f] = 0.0f;
+  for (int u = 0; u < UNROLL; ++u) acc[u] = 0.0;
 
   const size_t tile = (size_t)kStreamThreads * UNROLL;
   const size_t step = (size_t)gridDim.x * tile;
@@ -136,9 +146,7 @@ __global__ void __launch_bounds__(kStreamThreads) k_stream_sum(const float *__re
       for (int u = 0; u < UNROLL; ++u)
         v[u].load(body + (base + (size_t)u * kStreamThreads + threadIdx.x) * F);
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-        for (int f = 0; f < F; ++f) acc[u][f] += __uint_as_float(v[u].w[f]);
+      for (int u = 0; u < UNROLL; ++u) acc[u] += static_cast<double>(v[u].pairwise_sum());
     } else {
 #pragma unroll 1
       for (int u = 0; u < UNROLL; ++u) {
@@ -146,17 +154,14 @@ __global__ void __launch_bounds__(kStreamThreads) k_stream_sum(const float *__re
         if (i < nvec) {
           Vec<VB> v;
           v.load(body + i * F);
-#pragma unroll
-          for (int f = 0; f < F; ++f) acc[0][f] += __uint_as_float(v.w[f]);
+          acc[0] += static_cast<double>(v.pairwise_sum());
         }
       }
     }
   }
   double t = 0.0;
 #pragma unroll
-  for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-    for (int f = 0; f < F; ++f) t += static_cast<double>(acc[u][f]);
+  for (int u = 0; u < UNROLL; ++u) t += acc[u];
   if (blockIdx.x == 0) {
     for (size_t i = threadIdx.x; i < head; i += kStreamThreads) t += src[i];
     for (size_t i = head + nvec * F + threadIdx.x; i < n; i += kStreamThreads) t += src[i];
@@ -190,7 +195,7 @@ struct CopyConfig {
 };
 
 // Default launch shape of the copy stream.
-constexpr CopyConfig kCopyDefault = {32, 4, 4};
+constexpr CopyConfig kCopyDefault = {32, 2, 2};
 constexpr int kSumVec = 32, kSumUnroll = 4, kSumCtasPerSm = 4;
 
 int stream_grid(size_t units, size_t per_cta, int ctas_per_sm) {

@@ -123,6 +123,32 @@ int cmb_chase_run(const uint32_t *links, size_t words, uint64_t warmup, uint64_t
 int cmb_chase_host_walk(const uint32_t *host_links, size_t words, uint64_t hops,
                         uint32_t *out_index);
 
+/* --- TMA bulk-tensor tile movement (src/tma.cu) --------------------- */
+
+/* dst = src for a rows x cols row-major bf16 matrix, moved in box_rows x
+ * box_cols tiles by cp.async.bulk.tensor loads into a `stages`-deep
+ * shared-memory ring (mbarrier complete_tx) and tiled TMA stores back out;
+ * ctas_per_sm persistent CTAs per SM stride over the tiles.  Needs cols % 8
+ * == 0, 16-byte aligned bases, box dims in [1,256] x [8,256] with box bytes
+ * a multiple of 1024 and stages * box bytes <= 226 KiB.  Replaces
+ * kernel_tma_g2s_bandwidth (src/tma.cu:72-121), which loaded 16 KiB bulk
+ * chunks and discarded them, with a verifiable tile copy. */
+int cmb_tma_tile_copy_bf16(void *dst, const void *src, int rows, int cols, int box_rows,
+                           int box_cols, int stages, int ctas_per_sm, int *status,
+                           cmb_stream_t stream);
+/* Load-only form of the same pipeline (the reference's read-only G2S
+ * bandwidth, src/tma.cu:72-121,247): one CTA per SM (at most xor_words);
+ * CTA b writes to xor_out[b] the XOR of the first four 32-bit words of every
+ * tile it loaded (tiles b, b + grid, ...; the other entries are zeroed). */
+int cmb_tma_tile_load_bf16(const void *src, int rows, int cols, int box_rows, int box_cols,
+                           int stages, uint32_t *xor_out, size_t xor_words, int *status,
+                           cmb_stream_t stream);
+/* One thread issues `iters` 16-byte 1-D TMA loads of buf, waiting for each;
+ * *out_cycles (device) = SM cycles of the loop.  Replaces
+ * kernel_tma_1d_latency (src/tma.cu:20-69). */
+int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint32_t *out_cycles,
+                       int *status, cmb_stream_t stream);
+
 /* --- results table (include/result_logger.h, src/result_logger.cu) --- */
 
 /* Same meaning as ResultLogger::setDevice (include/result_logger.h:113-121). */
