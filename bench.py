@@ -402,6 +402,121 @@ def probe_chase(torch, stream, sh, hops):
             "endpoint_matches_host_walk": idx == expect}
 
 
+def probe_tma(torch, stream, sh, peaks):
+    """Config: 16384 x 16384 bf16 N(0,1), 128x128 boxes, 4-stage mbarrier
+    ring, TMA store; bit-exact.  Also the load-only pipeline (the reference's
+    tma_g2s_load_bw_gibps) and the 16-byte 1-D TMA round trip."""
+    from cuda_micro_bench_b200 import check
+
+    n = 16384
+    src = torch.empty(n * n, dtype=torch.int16, device="cuda")
+    dst = torch.zeros_like(src)
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(src.data_ptr()), n * n, ctypes.c_uint64(SEED),
+          ctypes.c_float(1.0), sh)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    xor = torch.zeros(4096, dtype=torch.int32, device="cuda")
+    out = {}
+    for label, stages, ctas in (("tile_copy_4stage", 4, 1), ("tile_copy_3stage", 3, 1)):
+        fn = lambda: check("cmb_tma_tile_copy_bf16", ctypes.c_void_p(dst.data_ptr()),
+                           ctypes.c_void_p(src.data_ptr()), n, n, 128, 128, stages, ctas,
+                           ctypes.c_void_p(status.data_ptr()), sh)
+        ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+        gbs = 2.0 * 2 * n * n / (ms * 1e-3) / 1e9
+        out[label] = {"GB/s": round(gbs, 2), "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                      "frac_of_8tbs_spec": round(gbs / 8000.0, 4), "stages": stages, "box": [128, 128],
+                      "bit_exact": bool(torch.equal(src, dst)), "status": int(status.item()),
+                      "ms": round(ms, 4)}
+    fn = lambda: check("cmb_tma_tile_load_bf16", ctypes.c_void_p(src.data_ptr()), n, n, 128, 128,
+                       4, ctypes.c_void_p(xor.data_ptr()), 4096,
+                       ctypes.c_void_p(status.data_ptr()), sh)
+    ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+    gbs = 2.0 * n * n / (ms * 1e-3) / 1e9
+    out["load_only_4stage"] = {"GB/s": round(gbs, 2), "GiB/s": round(gbs / 1.073741824, 2),
+                               "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                               "status": int(status.item())}
+    buf = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    cyc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    check("cmb_tma_1d_latency", ctypes.c_void_p(buf.data_ptr()), 1024, 256,
+          ctypes.c_void_p(cyc.data_ptr()), ctypes.c_void_p(status.data_ptr()), sh)
+    torch.cuda.synchronize()
+    out["tma_1d_load_latency_cyc"] = int(cyc.item()) / 256
+    del src, dst
+    return out
+
+
+def probe_gemm(torch, stream, sh, peaks):
+    """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5, fp32 accumulation in
+    TMEM, 2-CTA 256x256 tiles (and the 1-CTA 128x256 form); FP8 e4m3 with a
+    per-tensor scale.  TFLOP/s = 2*M*N*K / median launch time; 8 sampled
+    64x64 output tiles are checked against an fp64 product."""
+    from cuda_micro_bench_b200 import check
+
+    M = N = K = 8192
+    flop = 2.0 * M * N * K
+    A = torch.empty(M * K, dtype=torch.int16, device="cuda")
+    B = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(A.data_ptr()), M * K, ctypes.c_uint64(SEED + 1),
+          ctypes.c_float(K ** -0.5), sh)
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(B.data_ptr()), N * K, ctypes.c_uint64(SEED + 2),
+          ctypes.c_float(K ** -0.5), sh)
+    C = torch.empty(M * N, dtype=torch.float32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qa = torch.empty(M * K, dtype=torch.uint8, device="cuda")
+    qb = torch.empty(N * K, dtype=torch.uint8, device="cuda")
+    sa = torch.zeros(2, dtype=torch.float32, device="cuda")
+    sb = torch.zeros(2, dtype=torch.float32, device="cuda")
+    check("cmb_quantize_e4m3", ctypes.c_void_p(A.data_ptr()), M * K, ctypes.c_void_p(qa.data_ptr()),
+          ctypes.c_void_p(sa.data_ptr()), sh)
+    check("cmb_quantize_e4m3", ctypes.c_void_p(B.data_ptr()), N * K, ctypes.c_void_p(qb.data_ptr()),
+          ctypes.c_void_p(sb.data_ptr()), sh)
+    g = torch.Generator().manual_seed(3)
+    rows = torch.randint(0, M // 64, (8,), generator=g) * 64
+    cols = torch.randint(0, N // 64, (8,), generator=g) * 64
+
+    def sampled_err(a_f64, b_f64):
+        Cm = C.view(M, N)
+        worst = 0.0
+        for r, c in zip(rows.tolist(), cols.tolist()):
+            ref = a_f64[r:r + 64] @ b_f64[c:c + 64].T
+            got = Cm[r:r + 64, c:c + 64].double()
+            worst = max(worst, float((got - ref).abs().max() / ref.abs().max()))
+        return worst
+
+    a64 = A.view(M, K).view(torch.bfloat16).double()
+    b64 = B.view(N, K).view(torch.bfloat16).double()
+    out = {}
+    for label, cg in (("bf16_8192_2cta", 2), ("bf16_8192_1cta", 1)):
+        fn = lambda: check("cmb_gemm_bf16", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
+                           ctypes.c_void_p(C.data_ptr()), M, N, K, cg,
+                           ctypes.c_void_p(status.data_ptr()), sh)
+        ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+        tf = flop / (ms * 1e-3) / 1e12
+        err = sampled_err(a64, b64)
+        out[label] = {"TFLOP/s": round(tf, 1), "frac_of_measured_bf16": round(tf / peaks["bf16_tflops"], 4),
+                      "frac_of_2250_spec": round(tf / 2250.0, 4), "ms": round(ms, 4),
+                      "sampled_tiles_max_rel_err": err, "within_1e-2": err <= 1e-2,
+                      "status": int(status.item())}
+    del a64, b64
+
+    def deq(q, s, rows_, cols_):
+        return q.view(rows_, cols_).view(torch.float8_e4m3fn).double() * float(s[0].item())
+
+    a8, b8 = deq(qa, sa, M, K), deq(qb, sb, N, K)
+    for label, cg in (("fp8_e4m3_8192_2cta", 2), ("fp8_e4m3_8192_1cta", 1)):
+        fn = lambda: check("cmb_gemm_e4m3", ctypes.c_void_p(qa.data_ptr()), ctypes.c_void_p(qb.data_ptr()),
+                           ctypes.c_void_p(C.data_ptr()), M, N, K, ctypes.c_void_p(sa.data_ptr()),
+                           ctypes.c_void_p(sb.data_ptr()), cg, ctypes.c_void_p(status.data_ptr()), sh)
+        ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+        tf = flop / (ms * 1e-3) / 1e12
+        err = sampled_err(a8, b8)
+        out[label] = {"TFLOP/s": round(tf, 1), "frac_of_4500_spec": round(tf / 4500.0, 4),
+                      "frac_of_2x_measured_bf16": round(tf / (2 * peaks["bf16_tflops"]), 4),
+                      "ms": round(ms, 4), "sampled_tiles_max_rel_err": err,
+                      "within_1e-2": err <= 1e-2, "status": int(status.item())}
+    del A, B, C, qa, qb, a8, b8
+    return out
+
+
 def run_probes(args, ranks, peaks) -> dict:
     import torch
 
@@ -411,6 +526,10 @@ def run_probes(args, ranks, peaks) -> dict:
     if ranks.world == 1:
         out.update(probe_stream_1gib(torch, stream, sh, peaks))
         out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (24 if args.full_chase else 22))
+        torch.cuda.empty_cache()
+        out["tma_16384"] = probe_tma(torch, stream, sh, peaks)
+        torch.cuda.empty_cache()
+        out["gemm"] = probe_gemm(torch, stream, sh, peaks)
     torch.cuda.empty_cache()
     return out
 

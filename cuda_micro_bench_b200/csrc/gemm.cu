@@ -1,0 +1,399 @@
+// gemm.cu — tcgen05 dense GEMM probes, BF16 and FP8 E4M3 (the tensor-core
+// probes of the reference, src/tensor_core.cu and
+// src/tensor_core_extended.cu, re-targeted from register-only mma.sync
+// chains to a full GEMM on the 5th-generation tensor core).
+//
+// C[M x N] (fp32, row-major) = scale * A[M x K] * B[N x K]^T, A and B
+// K-major ("row.col", src/tensor_core_extended.cu:116).
+//
+// Structure (one CTA per SM, persistent, 192 threads):
+//   warp 0      TMA producer: 128-byte-swizzled K-major tiles of A and B
+//               into a STAGES-deep shared-memory ring (full/empty mbarriers)
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma for each 128-byte K slice (4 instructions of
+//               K = 32 bytes), tcgen05.commit frees the smem stage and, after
+//               the last K block, marks the accumulator full
+//   warps 2-5   epilogue: tcgen05.ld 32x32b from the accumulator, scale,
+//               streaming stores of fp32 C; two TMEM accumulators (2 x 256
+//               columns) let the epilogue of tile j overlap the MMAs of j+1.
+// CG = 1: tile 128 x 256 per CTA (cta_group::1, MMA M=128 N=256).
+// CG = 2: a cluster of two CTAs computes a 256 x 256 tile with
+//   cta_group::2 MMAs (M=256 N=256) issued by CTA 0; each CTA loads its own
+//   128 rows of A and 128 rows of B (N), the loads of both CTAs complete on
+//   CTA 0's full barrier, and CTA 0 commits to both CTAs' barriers one
+//   address at a time.
+// All waits are bounded; a wait that gives up reports CMB_ERR_TIMEOUT in
+// `status` and every role drains and leaves.
+#include <cuda.h>
+#include <cuda_fp8.h>
+
+#include "cmb_device.cuh"
+#include "cmb_host.h"
+#include "tcgen05.cuh"
+
+namespace cmb {
+
+int make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t rows,
+                 uint64_t cols, uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols,
+                 CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo);
+
+namespace {
+
+template <int CG, bool kFp8>
+struct GemmCfg {
+  static constexpr int kThreads = 192;
+  static constexpr int kBmCta = 128;                 // A rows per CTA
+  static constexpr int kBn = 256;                    // MMA N = output columns per tile
+  static constexpr int kBnCta = kBn / CG;            // B rows loaded per CTA
+  static constexpr int kKBytes = 128;                // K bytes per stage (one swizzle row)
+  static constexpr int kElem = kFp8 ? 1 : 2;
+  static constexpr int kBk = kKBytes / kElem;        // K elements per stage
+  static constexpr int kMmaPerStage = 4;             // 32 bytes of K per instruction
+  static constexpr int kABytes = kBmCta * kKBytes;   // 16 KiB
+  static constexpr int kBBytes = kBnCta * kKBytes;   // 32 KiB (CG=1) / 16 KiB (CG=2)
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = CG == 1 ? 4 : 6;
+  static constexpr int kTileM = kBmCta * CG;         // output rows per tile
+  static constexpr int kTmemCols = 512;              // two 256-column accumulators
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+  static constexpr uint32_t kIdesc = tc::instr_desc<kTileM, kBn, kFp8>();
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int &tm,
+                                            int &tn) {
+  // Grouped raster: group_m tile rows advance together along N, so the CTAs
+  // working at the same time share A rows and B columns in L2.
+  const int per_group = group_m * tiles_n;
+  const int g = t / per_group;
+  const int first = g * group_m;
+  const int gsize = min(tiles_m - first, group_m);
+  const int r = t - g * per_group;
+  tm = first + r % gsize;
+  tn = r / gsize;
+}
+
+__device__ __forceinline__ void st_cs_f4(float *p, float a, float b, float c, float d) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+template <int CG, bool kFp8>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+           float *__restrict__ C, int M, int N, int K, const float *scale_a,
+           const float *scale_b, int group_m, int *status) {
+  using Cfg = GemmCfg<CG, kFp8>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[Cfg::kStages], empty[Cfg::kStages];
+  __shared__ __align__(8) uint64_t tfull[2], tempty[2], mma_done;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? tc::cluster_ctarank() : 0u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      dev::mbar_init(dev::smem_addr(&full[s]), 1);
+      dev::mbar_init(dev::smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      dev::mbar_init(dev::smem_addr(&tfull[a]), 1);
+      dev::mbar_init(dev::smem_addr(&tempty[a]), 4 * CG);
+    }
+    dev::mbar_init(dev::smem_addr(&mma_done), 1);
+    abort_flag = 0;
+    dev::fence_mbar_init();
+    dev::tma_prefetch_desc(&tmA);
+    dev::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc<CG>(dev::smem_addr(&tmem_holder), Cfg::kTmemCols);
+    tc::tmem_relinquish<CG>();
+  }
+  tc::fence_before_sync();
+  if constexpr (CG == 2) tc::cluster_sync();
+  else __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem_base = tmem_holder;
+
+  const int tiles_m = (M + Cfg::kTileM - 1) / Cfg::kTileM;
+  const int tiles_n = (N + Cfg::kBn - 1) / Cfg::kBn;
+  const int tiles = tiles_m * tiles_n;
+  const int cluster = blockIdx.x / CG, nclusters = gridDim.x / CG;
+  const int kblocks = (K + Cfg::kBk - 1) / Cfg::kBk;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster; t < tiles && ok; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
+        const int a_row = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta;
+        const int b_row = tn * Cfg::kBn + static_cast<int>(rank) * Cfg::kBnCta;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % Cfg::kStages;
+          const uint32_t ph = (it / Cfg::kStages) & 1;
+          if (!dev::mbar_wait_bounded(dev::smem_addr(&empty[s]), ph ^ 1) ||
+              *(volatile int *)&abort_flag) {
+            dev::report_status(status, CMB_ERR_TIMEOUT);
+            atomicExch(&abort_flag, 1);
+            ok = false;
+            break;
+          }
+          uint8_t *a_dst = ring + (size_t)s * Cfg::kStageBytes;
+          uint8_t *b_dst = a_dst + Cfg::kABytes;
+          const int kx = kb * Cfg::kBk;
+          const uint32_t bar = dev::smem_addr(&full[s]);
+          if constexpr (CG == 1) {
+            dev::mbar_arrive_expect_tx(bar, Cfg::kStageBytes);
+            dev::tma_load_2d(dev::smem_addr(a_dst), &tmA, kx, a_row, bar);
+            dev::tma_load_2d(dev::smem_addr(b_dst), &tmB, kx, b_row, bar);
+          } else {
+            const uint32_t leader_bar = tc::map_to_cta(bar, 0);
+            if (rank == 0) dev::mbar_arrive_expect_tx(bar, 2 * Cfg::kStageBytes);
+            tc::tma_load_2d_pair(dev::smem_addr(a_dst), &tmA, kx, a_row, leader_bar);
+            tc::tma_load_2d_pair(dev::smem_addr(b_dst), &tmB, kx, b_row, leader_bar);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // --------------------------------------------------------- MMA issuer
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = cluster; t < tiles && ok; t += nclusters, ++j) {
+        const int a = j & 1;
+        const uint32_t aph = (j >> 1) & 1;
+        if (!dev::mbar_wait_bounded(dev::smem_addr(&tempty[a]), aph ^ 1)) {
+          dev::report_status(status, CMB_ERR_TIMEOUT);
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(a * Cfg::kBn);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % Cfg::kStages;
+          const uint32_t ph = (it / Cfg::kStages) & 1;
+          if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), ph) ||
+              *(volatile int *)&abort_flag) {
+            dev::report_status(status, CMB_ERR_TIMEOUT);
+            atomicExch(&abort_flag, 1);
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t a_addr = dev::smem_addr(ring + (size_t)s * Cfg::kStageBytes);
+          const uint64_t da = tc::sw128_kmajor_desc(a_addr);
+          const uint64_t db = tc::sw128_kmajor_desc(a_addr + Cfg::kABytes);
+#pragma unroll
+          for (int k = 0; k < Cfg::kMmaPerStage; ++k)
+            tc::mma<CG, kFp8>(d, da + 2 * k, db + 2 * k, Cfg::kIdesc, (kb | k) != 0 ? 1u : 0u);
+          const uint32_t eb = dev::smem_addr(&empty[s]);
+          tc::commit<CG>(eb);
+          if constexpr (CG == 2) tc::commit<CG>(tc::map_to_cta(eb, 1));
+        }
+        if (!ok) break;
+        const uint32_t fb = dev::smem_addr(&tfull[a]);
+        tc::commit<CG>(fb);
+        if constexpr (CG == 2) tc::commit<CG>(tc::map_to_cta(fb, 1));
+      }
+      // All MMAs this thread issued have completed once mma_done flips.
+      tc::commit<CG>(dev::smem_addr(&mma_done));
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&mma_done), 0))
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    float scale = 1.0f;
+    if constexpr (kFp8) scale = __ldg(scale_a) * __ldg(scale_b);
+    const bool vec_ok = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    int j = 0;
+    for (int t = cluster; t < tiles; t += nclusters, ++j) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
+      const int a = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&tfull[a]), ph) ||
+          *(volatile int *)&abort_flag) {
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+        atomicExch(&abort_flag, 1);
+        break;
+      }
+      tc::fence_after_sync();
+      const int row = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta + q * 32 + lane;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * Cfg::kBn);
+      float *crow = C + (size_t)row * N;
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kBn / 32; ++c) {
+        uint32_t r[32];
+        tc::ld_32x32b_x32(taddr + c * 32, r);
+        tc::wait_ld();
+        const int col0 = tn * Cfg::kBn + c * 32;
+        if (row < M) {
+          if (vec_ok && col0 + 32 <= N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              st_cs_f4(crow + col0 + i, scale * __uint_as_float(r[i]),
+                       scale * __uint_as_float(r[i + 1]), scale * __uint_as_float(r[i + 2]),
+                       scale * __uint_as_float(r[i + 3]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < N) crow[col0 + i] = scale * __uint_as_float(r[i]);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t eb = dev::smem_addr(&tempty[a]);
+        if constexpr (CG == 1) dev::mbar_arrive(eb);
+        else dev::mbar_arrive_cluster(tc::map_to_cta(eb, 0));
+      }
+    }
+  }
+
+  // ------------------------------------------------------------- teardown
+  tc::fence_before_sync();
+  __syncthreads();
+  if constexpr (CG == 2) tc::cluster_sync();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc<CG>(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------ e4m3 quantisation
+
+__global__ void k_amax_bf16(const __nv_bfloat16 *__restrict__ x, size_t n, float *amax) {
+  float m = 0.0f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(__bfloat162float(x[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  // non-negative floats order like their bit patterns
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned int *>(amax), __float_as_uint(m));
+}
+
+// q = e4m3_satfinite(x * (448 / amax)); scale_out[0] = amax / 448 (the
+// factor that turns q back into x).
+__global__ void k_quantize_e4m3(const __nv_bfloat16 *__restrict__ x, size_t n,
+                                __nv_fp8_storage_t *__restrict__ q, float *scale_out) {
+  const float amax = scale_out[1];
+  const float inv = amax > 0.0f ? __fdiv_rn(448.0f, amax) : 1.0f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    q[i] = __nv_cvt_float_to_fp8(__fmul_rn(__bfloat162float(x[i]), inv), __NV_SATFINITE,
+                                 __NV_E4M3);
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    scale_out[0] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+}
+
+template <int CG, bool kFp8>
+int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
+                const float *scale_a, const float *scale_b, int *status, cudaStream_t stream) {
+  using Cfg = GemmCfg<CG, kFp8>;
+  const CUtensorMapDataType dt =
+      kFp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, dt, A, M, K, (uint64_t)K * Cfg::kElem, Cfg::kBmCta, Cfg::kBk,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, dt, B, N, K, (uint64_t)K * Cfg::kElem, Cfg::kBnCta, Cfg::kBk,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (rc) return rc;
+  auto kern = k_gemm<CG, kFp8>;
+  CMB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(Cfg::kSmem)));
+  const int tiles = ((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kBn - 1) / Cfg::kBn);
+  int clusters = current_sm_count() / CG;
+  if (clusters > tiles) clusters = tiles;
+  const int group_m = CG == 1 ? 16 : 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * CG));
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CMB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, C, M, N, K, scale_a, scale_b, group_m,
+                                  status));
+  return CMB_OK;
+}
+
+int gemm_checks(const char *fn, const void *A, const void *B, const float *C, int M, int N, int K,
+                int elem, int cta_group) {
+  if (A == nullptr || B == nullptr || C == nullptr)
+    return fail(CMB_ERR_INVALID_ARG, "%s: null operand", fn);
+  if (M <= 0 || N <= 0 || K <= 0) return fail(CMB_ERR_INVALID_ARG, "%s: empty GEMM", fn);
+  if ((static_cast<long long>(K) * elem) % 16 != 0)
+    return fail(CMB_ERR_INVALID_ARG, "%s: K*%d bytes must be a multiple of 16", fn, elem);
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return fail(CMB_ERR_INVALID_ARG, "%s: A and B must be 16-byte aligned", fn);
+  if (cta_group != 1 && cta_group != 2)
+    return fail(CMB_ERR_INVALID_ARG, "%s: cta_group %d not 1 or 2", fn, cta_group);
+  if (current_cc() != 100)
+    return fail(CMB_ERR_UNSUPPORTED, "%s: needs an sm_100 device (found cc %d)", fn, current_cc());
+  return CMB_OK;
+}
+
+}  // namespace
+}  // namespace cmb
+
+using namespace cmb;
+
+extern "C" int cmb_gemm_bf16(const void *A, const void *B, float *C, int M, int N, int K,
+                             int cta_group, int *status, cmb_stream_t stream) {
+  int rc = gemm_checks("cmb_gemm_bf16", A, B, C, M, N, K, 2, cta_group);
+  if (rc) return rc;
+  if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
+  return cta_group == 1
+             ? launch_gemm<1, false>(A, B, C, M, N, K, nullptr, nullptr, status, stream)
+             : launch_gemm<2, false>(A, B, C, M, N, K, nullptr, nullptr, status, stream);
+}
+
+extern "C" int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
+                             const float *scale_a, const float *scale_b, int cta_group,
+                             int *status, cmb_stream_t stream) {
+  int rc = gemm_checks("cmb_gemm_e4m3", A, B, C, M, N, K, 1, cta_group);
+  if (rc) return rc;
+  if (scale_a == nullptr || scale_b == nullptr)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_e4m3: null scale");
+  if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
+  return cta_group == 1
+             ? launch_gemm<1, true>(A, B, C, M, N, K, scale_a, scale_b, status, stream)
+             : launch_gemm<2, true>(A, B, C, M, N, K, scale_a, scale_b, status, stream);
+}
+
+extern "C" int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst,
+                                 float *scale_out, cmb_stream_t stream) {
+  if (src_bf16 == nullptr || dst == nullptr || scale_out == nullptr)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_quantize_e4m3: null pointer");
+  CMB_CUDA_TRY(cudaMemsetAsync(scale_out, 0, 2 * sizeof(float), stream));
+  if (n == 0) return CMB_OK;
+  size_t grid = (n + 255) / 256;
+  const size_t cap = static_cast<size_t>(current_sm_count()) * 8;
+  if (grid > cap) grid = cap;
+  const auto *x = reinterpret_cast<const __nv_bfloat16 *>(src_bf16);
+  k_amax_bf16<<<static_cast<int>(grid), 256, 0, stream>>>(x, n, scale_out + 1);
+  CMB_LAUNCH_CHECK();
+  k_quantize_e4m3<<<static_cast<int>(grid), 256, 0, stream>>>(
+      x, n, reinterpret_cast<__nv_fp8_storage_t *>(dst), scale_out);
+  CMB_LAUNCH_CHECK();
+  return CMB_OK;
+}

@@ -149,6 +149,31 @@ int cmb_tma_tile_load_bf16(const void *src, int rows, int cols, int box_rows, in
 int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint32_t *out_cycles,
                        int *status, cmb_stream_t stream);
 
+/* --- tcgen05 dense GEMM (src/tensor_core.cu, src/tensor_core_extended.cu)  */
+
+/* C[M x N] (fp32, row-major) = A[M x K] * B[N x K]^T for bf16 A, B stored
+ * K-major (row-major with K contiguous; the "row.col" operand order of
+ * src/tensor_core_extended.cu:116), fp32 accumulation in tensor memory.
+ * cta_group 1: 128 x 256 tiles per CTA; 2: 256 x 256 tiles per pair of CTAs
+ * (cta_group::2 MMAs).  Needs K % 8 == 0 and 16-byte aligned A, B.
+ * Replaces the register-only mma.sync throughput kernels
+ * (src/tensor_core_extended.cu:77-128,265-292) with a GEMM that reads and
+ * writes memory and has a checkable result. */
+int cmb_gemm_bf16(const void *A, const void *B, float *C, int M, int N, int K, int cta_group,
+                  int *status, cmb_stream_t stream);
+/* Same for e4m3 A, B (K % 16 == 0): C = (*scale_a) * (*scale_b) * A * B^T,
+ * scales read from device memory.  Replaces the FP8 mma.sync kernels
+ * (src/tensor_core_extended.cu:133-184). */
+int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
+                  const float *scale_a, const float *scale_b, int cta_group, int *status,
+                  cmb_stream_t stream);
+/* Per-tensor e4m3 quantisation of n bf16 values: amax = max |x|,
+ * dst[i] = e4m3_satfinite(x[i] * (448 / amax)) (fp32 multiply, round to
+ * nearest even), scale_out[0] = amax / 448 (the dequantisation factor),
+ * scale_out[1] = amax; scale_out is device memory of 2 floats. */
+int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst, float *scale_out,
+                      cmb_stream_t stream);
+
 /* --- results table (include/result_logger.h, src/result_logger.cu) --- */
 
 /* Same meaning as ResultLogger::setDevice (include/result_logger.h:113-121). */

@@ -1,0 +1,136 @@
+"""GPU parity of the tcgen05 GEMM probes against the oracle's fp64 GEMM
+(stated tolerance: per checked tile, max |C - C_ref| <= 1e-2 * max |C_ref|),
+and of the e4m3 quantiser against the oracle's encoder (bit-exact)."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import ptr
+from tests.helpers import dptr, stream_handle
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-2  # stated GEMM tolerance (max-norm, per tile)
+
+
+def _normal_bf16(cuda, cmb, rows, cols, seed, scale):
+    t = cuda.empty(rows * cols, dtype=cuda.int16, device="cuda")
+    cmb.check("cmb_fill_normal_bf16", dptr(t), rows * cols, ctypes.c_uint64(seed),
+              ctypes.c_float(scale), stream_handle(cuda))
+    return t
+
+
+def _gemm(cuda, cmb, fn, A, B, M, N, K, cg, scales=None):
+    C = cuda.full((M * N,), float("nan"), dtype=cuda.float32, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    if fn == "bf16":
+        cmb.check("cmb_gemm_bf16", dptr(A), dptr(B), dptr(C), M, N, K, cg, dptr(status),
+                  stream_handle(cuda))
+    else:
+        cmb.check("cmb_gemm_e4m3", dptr(A), dptr(B), dptr(C), M, N, K, dptr(scales[0]),
+                  dptr(scales[1]), cg, dptr(status), stream_handle(cuda))
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0, "a device-side wait timed out"
+    return C.cpu().numpy().reshape(M, N)
+
+
+def _check_tiles(orc, A_h, B_h, C, K, tiles, dtype=0, sa=1.0, sb=1.0):
+    worst = 0.0
+    for (r0, c0, tm, tn) in tiles:
+        ref = np.empty((tm, tn), np.float64)
+        orc.orc_gemm_tile_f64(ptr(A_h), ptr(B_h), dtype, K, K, K, r0, c0, tm, tn, sa, sb, ptr(ref))
+        got = C[r0:r0 + tm, c0:c0 + tn].astype(np.float64)
+        assert np.isfinite(got).all()
+        err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
+        worst = max(worst, err)
+        assert err <= RTOL, (r0, c0, err)
+    return worst
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (256, 512, 1024), (200, 136, 72),
+                                   (1000, 700, 520), (128, 256, 8)])
+def test_gemm_bf16_small_full_check(cuda, cmb, orc, cg, M, N, K):
+    A = _normal_bf16(cuda, cmb, M, K, 1, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 2, K ** -0.5)
+    C = _gemm(cuda, cmb, "bf16", A, B, M, N, K, cg)
+    A_h = A.cpu().numpy().view(np.uint16)
+    B_h = B.cpu().numpy().view(np.uint16)
+    worst = _check_tiles(orc, A_h, B_h, C, K, [(0, 0, M, N)])
+    assert worst < 1e-4  # fp32 accumulation of exact bf16 products
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+def test_gemm_bf16_8192_sampled_tiles(cuda, cmb, orc, cg):
+    """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5; 64 sampled 64x64 output
+    tiles against the fp64 oracle."""
+    M = N = K = 8192
+    A = _normal_bf16(cuda, cmb, M, K, 11, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 12, K ** -0.5)
+    C = _gemm(cuda, cmb, "bf16", A, B, M, N, K, cg)
+    A_h = A.cpu().numpy().view(np.uint16)
+    B_h = B.cpu().numpy().view(np.uint16)
+    rng = np.random.default_rng(cg)
+    tiles = [(int(r) * 64, int(c) * 64, 64, 64)
+             for r, c in zip(rng.integers(0, M // 64, 64), rng.integers(0, N // 64, 64))]
+    tiles[0] = (0, 0, 64, 64)
+    tiles[1] = (M - 64, N - 64, 64, 64)
+    worst = _check_tiles(orc, A_h, B_h, C, K, tiles)
+    assert worst < 1e-4
+    assert np.isfinite(C).all()
+
+
+def _quantize(cuda, cmb, x):
+    q = cuda.empty(x.numel(), dtype=cuda.uint8, device="cuda")
+    sc = cuda.zeros(2, dtype=cuda.float32, device="cuda")
+    cmb.check("cmb_quantize_e4m3", dptr(x), x.numel(), dptr(q), dptr(sc), stream_handle(cuda))
+    return q, sc
+
+
+def test_quantize_e4m3_matches_oracle(cuda, cmb, orc):
+    n = 1 << 20
+    x = _normal_bf16(cuda, cmb, 1, n, 5, 3.0)
+    q, sc = _quantize(cuda, cmb, x)
+    x_h = x.cpu().numpy().view(np.uint16)
+    amax = orc.orc_amax_bf16(ptr(x_h), n)
+    s = sc.cpu().numpy()
+    assert s[1] == np.float32(amax)
+    assert s[0] == np.float32(amax) / np.float32(448.0)
+    inv = np.float32(448.0) / np.float32(amax)
+    ref = np.empty(n, np.uint8)
+    orc.orc_quantize_e4m3(ptr(x_h), n, float(inv), ptr(ref))
+    assert np.array_equal(q.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (384, 520, 1040), (8192, 8192, 8192)])
+def test_gemm_e4m3(cuda, cmb, orc, cg, M, N, K):
+    """Config (largest case): the 8192^3 GEMM with A, B quantised to e4m3 with
+    a per-tensor scale; checked against fp64 on the dequantised inputs."""
+    A = _normal_bf16(cuda, cmb, M, K, 21, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 22, K ** -0.5)
+    qa, sa = _quantize(cuda, cmb, A)
+    qb, sb = _quantize(cuda, cmb, B)
+    C = _gemm(cuda, cmb, "e4m3", qa, qb, M, N, K, cg, scales=(sa[:1], sb[:1]))
+    qa_h, qb_h = qa.cpu().numpy(), qb.cpu().numpy()
+    sa_h, sb_h = float(sa[0].item()), float(sb[0].item())
+    if M * N <= 1 << 20:
+        tiles = [(0, 0, M, N)]
+    else:
+        rng = np.random.default_rng(7 + cg)
+        tiles = [(int(r) * 64, int(c) * 64, 64, 64)
+                 for r, c in zip(rng.integers(0, M // 64, 64), rng.integers(0, N // 64, 64))]
+    _check_tiles(orc, qa_h, qb_h, C, K, tiles, dtype=1, sa=sa_h, sb=sb_h)
+
+
+def test_gemm_rejects_bad_args(cuda, cmb):
+    a = cuda.zeros(1024, dtype=cuda.int16, device="cuda")
+    c = cuda.zeros(1024, dtype=cuda.float32, device="cuda")
+    s = stream_handle(cuda)
+    assert cmb.lib.cmb_gemm_bf16(dptr(a), dptr(a), dptr(c), 16, 16, 12, 1, None, s) == 1  # K%8
+    assert cmb.lib.cmb_gemm_bf16(dptr(a), dptr(a), dptr(c), 16, 16, 16, 3, None, s) == 1  # cg
+    assert cmb.lib.cmb_gemm_bf16(dptr(a), dptr(a), dptr(c), 0, 16, 16, 1, None, s) == 1
+    assert cmb.lib.cmb_gemm_e4m3(dptr(a), dptr(a), dptr(c), 16, 16, 16, None, None, 1, None,
+                                 s) == 1
