@@ -517,6 +517,29 @@ def probe_gemm(torch, stream, sh, peaks):
     return out
 
 
+def run_probe_only(args) -> int:
+    """Runs only the named probes (for profiling) and prints their results."""
+    import torch
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    stream = torch.cuda.current_stream()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    peaks = measured_peaks()
+    out = {}
+    for name in args.probe:
+        if name == "stream":
+            out.update(probe_stream_1gib(torch, stream, sh, peaks))
+        elif name == "chase":
+            out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (24 if args.full_chase else 22))
+        elif name == "tma":
+            out["tma_16384"] = probe_tma(torch, stream, sh, peaks)
+        elif name == "gemm":
+            out["gemm"] = probe_gemm(torch, stream, sh, peaks)
+        torch.cuda.empty_cache()
+    print(json.dumps({"probes": out}), flush=True)
+    return 0
+
+
 def run_probes(args, ranks, peaks) -> dict:
     import torch
 
@@ -570,6 +593,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-probes", action="store_true", help="headline only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--full-chase", action="store_true", help="2^24 chase hops (default 2^22)")
+    ap.add_argument("--probe", action="append", choices=["stream", "chase", "tma", "gemm"],
+                    help="run only this probe (repeatable); no headline line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -578,6 +603,8 @@ def main(argv=None) -> int:
         ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     if args.impl == "reference":
         return run_reference(args)
+    if args.probe:
+        return run_probe_only(args)
     return run_ours(args)
 
 
