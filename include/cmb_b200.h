@@ -87,6 +87,27 @@ size_t cmb_stream_sum_workspace_bytes(size_t n);
 int cmb_stream_sum_f32(const float *src, size_t n, double *out_sum, void *workspace,
                        size_t workspace_bytes, cmb_stream_t stream);
 
+/* The same sum without a caller-supplied workspace, for callers that cannot
+ * allocate device memory: code whose device memory is all owned by another
+ * allocator (a framework's caching allocator or a fixed arena), or
+ * latency-critical paths that cannot afford cudaMalloc/cudaFree, which may
+ * synchronise the device.  No counterpart in the reference.
+ * The workspace lives in a 33,024-byte array inside the library (one copy
+ * on every GPU that loads it, kept until the process exits): room for
+ * cmb_stream_sum_noalloc_max_ctas() = 4096 per-CTA partials.  The sum
+ * launches up to 4 CTAs per SM, so any n fits on GPUs of up to 1024 SMs;
+ * a GPU that would need more returns CMB_ERR_INVALID_ARG.  Nothing is
+ * allocated: no cudaMalloc, cudaFree or allocating library call.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  All calls on a device share the array: calls that overlap on
+ * the GPU (other streams, or other host threads) race and give wrong sums;
+ * serialise them.  The result equals cmb_stream_sum_f32's for the same
+ * input. */
+int cmb_stream_sum_f32_noalloc(const float *src, size_t n, double *out_sum, cmb_stream_t stream);
+/* Capacity of that array in per-CTA partials (4096). */
+size_t cmb_stream_sum_noalloc_max_ctas(void);
+
 /* Host-buffer stream copy: host_dst = host_src through the device.  Copies
  * chunks host->device, runs cmb_stream_copy on each, copies them back, with
  * the three steps of consecutive chunks overlapped on three streams.
