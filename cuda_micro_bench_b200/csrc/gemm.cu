@@ -14,8 +14,11 @@
 //               K = 32 bytes), tcgen05.commit frees the smem stage and, after
 //               the last K block, marks the accumulator full
 //   warps 2-5   epilogue: tcgen05.ld 32x32b from the accumulator, scale,
-//               streaming stores of fp32 C; two TMEM accumulators (2 x 256
-//               columns) let the epilogue of tile j overlap the MMAs of j+1.
+//               then either a 32 x 32 fp32 box per warp staged in swizzled
+//               shared memory and written by a tiled TMA store (default), or
+//               direct streaming stores (rows not TMA-addressable); two TMEM
+//               accumulators (2 x 256 columns) let the epilogue of tile j
+//               overlap the MMAs of tile j+1.
 // CG = 1: tile 128 x 256 per CTA (cta_group::1, MMA M=128 N=256).
 // CG = 2: a cluster of two CTAs computes a 256 x 256 tile with
 //   cta_group::2 MMAs (M=256 N=256) issued by CTA 0; each CTA loads its own
@@ -39,7 +42,7 @@ int make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, 
 
 namespace {
 
-template <int CG, bool kFp8>
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi>
 struct GemmCfg {
   static constexpr int kThreads = 192;
   static constexpr int kBmCta = 128;                 // A rows per CTA
@@ -52,10 +55,13 @@ struct GemmCfg {
   static constexpr int kABytes = kBmCta * kKBytes;   // 16 KiB
   static constexpr int kBBytes = kBnCta * kKBytes;   // 32 KiB (CG=1) / 16 KiB (CG=2)
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = CG == 1 ? 4 : 6;
+  static constexpr int kStages = STAGES;
   static constexpr int kTileM = kBmCta * CG;         // output rows per tile
   static constexpr int kTmemCols = 512;              // two 256-column accumulators
-  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+  // TMA-store epilogue: per epilogue warp two 32 x 32 fp32 staging boxes.
+  static constexpr int kEpiBoxBytes = 32 * 32 * 4;
+  static constexpr int kEpiBytes = kTmaEpi ? 4 * 2 * kEpiBoxBytes : 0;
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + kEpiBytes + 1024;
   static constexpr uint32_t kIdesc = tc::instr_desc<kTileM, kBn, kFp8>();
 };
 
@@ -78,12 +84,12 @@ __device__ __forceinline__ void st_cs_f4(float *p, float a, float b, float c, fl
                : "memory");
 }
 
-template <int CG, bool kFp8>
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi>
 __global__ void __launch_bounds__(192, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-           float *__restrict__ C, int M, int N, int K, const float *scale_a,
-           const float *scale_b, int group_m, int *status) {
-  using Cfg = GemmCfg<CG, kFp8>;
+           const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M, int N, int K,
+           const float *scale_a, const float *scale_b, int group_m, int *status) {
+  using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
@@ -109,6 +115,7 @@ __global__ void __launch_bounds__(192, 1)
     dev::fence_mbar_init();
     dev::tma_prefetch_desc(&tmA);
     dev::tma_prefetch_desc(&tmB);
+    if constexpr (kTmaEpi) dev::tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tc::tmem_alloc<CG>(dev::smem_addr(&tmem_holder), Cfg::kTmemCols);
@@ -215,6 +222,8 @@ __global__ void __launch_bounds__(192, 1)
     float scale = 1.0f;
     if constexpr (kFp8) scale = __ldg(scale_a) * __ldg(scale_b);
     const bool vec_ok = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    uint8_t *epi = ring + (size_t)Cfg::kStages * Cfg::kStageBytes + (size_t)q * 2 * Cfg::kEpiBoxBytes;
+    uint32_t epi_count = 0;
     int j = 0;
     for (int t = cluster; t < tiles; t += nclusters, ++j) {
       int tm, tn;
@@ -228,7 +237,8 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc::fence_after_sync();
-      const int row = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta + q * 32 + lane;
+      const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta + q * 32;
+      const int row = row0 + lane;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * Cfg::kBn);
       float *crow = C + (size_t)row * N;
@@ -237,8 +247,44 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t r[32];
         tc::ld_32x32b_x32(taddr + c * 32, r);
         tc::wait_ld();
+        if (c == Cfg::kBn / 32 - 1) {
+          // every TMEM read of this accumulator is done: hand it back
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t eb = dev::smem_addr(&tempty[a]);
+            if constexpr (CG == 1) dev::mbar_arrive(eb);
+            else dev::mbar_arrive_cluster(tc::map_to_cta(eb, 0));
+          }
+        }
         const int col0 = tn * Cfg::kBn + c * 32;
-        if (row < M) {
+        if constexpr (kTmaEpi) {
+          // Stage the warp's 32 x 32 box in shared memory (128-byte
+          // swizzle: 16-byte chunk j of row r at (j ^ (r % 8)) * 16, which
+          // also keeps the 8 lanes of each store phase on distinct banks)
+          // and write it out with one tiled TMA store.
+          uint8_t *box = epi + (size_t)(epi_count & 1) * Cfg::kEpiBoxBytes;
+          if (lane == 0) dev::bulk_wait_group_read<1>();  // the store 2 boxes ago has read it
+          __syncwarp();
+          const uint32_t rb = dev::smem_addr(box) + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t addr = rb + ((static_cast<uint32_t>(j) ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
+                         "f"(scale * __uint_as_float(r[4 * j])),
+                         "f"(scale * __uint_as_float(r[4 * j + 1])),
+                         "f"(scale * __uint_as_float(r[4 * j + 2])),
+                         "f"(scale * __uint_as_float(r[4 * j + 3]))
+                         : "memory");
+          }
+          dev::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < M && col0 < N) {
+            dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
+            dev::bulk_commit_group();
+          }
+          ++epi_count;
+        } else if (row < M) {
           if (vec_ok && col0 + 32 <= N) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
@@ -252,13 +298,10 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      tc::fence_before_sync();
+    }
+    if constexpr (kTmaEpi) {
+      if (lane == 0) dev::bulk_wait_group<0>();  // stores complete before the CTA leaves
       __syncwarp();
-      if (lane == 0) {
-        const uint32_t eb = dev::smem_addr(&tempty[a]);
-        if constexpr (CG == 1) dev::mbar_arrive(eb);
-        else dev::mbar_arrive_cluster(tc::map_to_cta(eb, 0));
-      }
     }
   }
 
@@ -299,10 +342,11 @@ __global__ void k_quantize_e4m3(const __nv_bfloat16 *__restrict__ x, size_t n,
     scale_out[0] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
 }
 
-template <int CG, bool kFp8>
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi>
 int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
-                const float *scale_a, const float *scale_b, int *status, cudaStream_t stream) {
-  using Cfg = GemmCfg<CG, kFp8>;
+                const float *scale_a, const float *scale_b, int group_m, int *status,
+                cudaStream_t stream) {
+  using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi>;
   const CUtensorMapDataType dt =
       kFp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta, tb;
@@ -312,13 +356,21 @@ int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
   rc = make_tmap_2d(&tb, dt, B, N, K, (uint64_t)K * Cfg::kElem, Cfg::kBnCta, Cfg::kBk,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
-  auto kern = k_gemm<CG, kFp8>;
+  CUtensorMap tcm;
+  if constexpr (kTmaEpi) {
+    rc = make_tmap_2d(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, (uint64_t)N * 4, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    if (rc) return rc;
+  } else {
+    tcm = ta;  // unused
+  }
+  auto kern = k_gemm<CG, kFp8, STAGES, kTmaEpi>;
   CMB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(Cfg::kSmem)));
   const int tiles = ((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kBn - 1) / Cfg::kBn);
   int clusters = current_sm_count() / CG;
   if (clusters > tiles) clusters = tiles;
-  const int group_m = CG == 1 ? 16 : 8;
+  if (group_m <= 0) group_m = 8;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(clusters * CG));
   cfg.blockDim = dim3(Cfg::kThreads);
@@ -331,8 +383,8 @@ int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CMB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, C, M, N, K, scale_a, scale_b, group_m,
-                                  status));
+  CMB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, C, M, N, K, scale_a, scale_b,
+                                  group_m, status));
   return CMB_OK;
 }
 
@@ -352,6 +404,50 @@ int gemm_checks(const char *fn, const void *A, const void *B, const float *C, in
   return CMB_OK;
 }
 
+// Default shapes (from sweeps on B200 against cuBLAS measured alongside):
+// 1-CTA 128x256 tiles with 4 stages of 48 KiB; 2-CTA 256x256 tiles with 4
+// stages of 32 KiB per CTA; raster groups of 8 tile rows; the TMA-store
+// epilogue whenever C's row pitch allows a tensor map (N % 4 == 0, 16-byte
+// aligned C).
+template <bool kFp8, bool kTmaEpi>
+int dispatch_stages(const void *A, const void *B, float *C, int M, int N, int K,
+                    const float *scale_a, const float *scale_b, int cta_group, int stages,
+                    int group_m, int *status, cudaStream_t stream) {
+#define CMB_GEMM_CASE(CGV, S)                                                                \
+  if (cta_group == CGV && stages == S)                                                      \
+    return launch_gemm<CGV, kFp8, S, kTmaEpi>(A, B, C, M, N, K, scale_a, scale_b, group_m,  \
+                                              status, stream);
+  if (stages == 0) stages = 4;
+  CMB_GEMM_CASE(1, 3)
+  CMB_GEMM_CASE(1, 4)
+  CMB_GEMM_CASE(2, 4)
+  CMB_GEMM_CASE(2, 5)
+  CMB_GEMM_CASE(2, 6)
+  if constexpr (!kTmaEpi) { CMB_GEMM_CASE(2, 7) }
+#undef CMB_GEMM_CASE
+  return fail(CMB_ERR_INVALID_ARG,
+              "gemm: stages %d not available for cta_group %d (1: 3-4; 2: 4-6, or 7 with the "
+              "direct-store epilogue)", stages, cta_group);
+}
+
+template <bool kFp8>
+int dispatch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
+                  const float *scale_a, const float *scale_b, int cta_group, int stages,
+                  int group_m, int epilogue, int *status, cudaStream_t stream) {
+  const bool tma_ok = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+  if (epilogue == 0) epilogue = tma_ok ? 2 : 1;
+  if (epilogue == 2 && !tma_ok)
+    return fail(CMB_ERR_INVALID_ARG, "gemm: the TMA-store epilogue needs N %% 4 == 0 and a "
+                "16-byte aligned C");
+  if (epilogue == 2)
+    return dispatch_stages<kFp8, true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, stages,
+                                       group_m, status, stream);
+  if (epilogue == 1)
+    return dispatch_stages<kFp8, false>(A, B, C, M, N, K, scale_a, scale_b, cta_group, stages,
+                                        group_m, status, stream);
+  return fail(CMB_ERR_INVALID_ARG, "gemm: epilogue %d not in {0, 1, 2}", epilogue);
+}
+
 }  // namespace
 }  // namespace cmb
 
@@ -362,9 +458,24 @@ extern "C" int cmb_gemm_bf16(const void *A, const void *B, float *C, int M, int 
   int rc = gemm_checks("cmb_gemm_bf16", A, B, C, M, N, K, 2, cta_group);
   if (rc) return rc;
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
-  return cta_group == 1
-             ? launch_gemm<1, false>(A, B, C, M, N, K, nullptr, nullptr, status, stream)
-             : launch_gemm<2, false>(A, B, C, M, N, K, nullptr, nullptr, status, stream);
+  return dispatch_gemm<false>(A, B, C, M, N, K, nullptr, nullptr, cta_group, 0, 0, 0, status,
+                              stream);
+}
+
+extern "C" int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int N, int K,
+                              int fp8, const float *scale_a, const float *scale_b, int cta_group,
+                              int stages, int group_m, int epilogue, int *status,
+                              cmb_stream_t stream) {
+  int rc = gemm_checks("cmb_gemm_tuned", A, B, C, M, N, K, fp8 ? 1 : 2, cta_group);
+  if (rc) return rc;
+  if (fp8 && (scale_a == nullptr || scale_b == nullptr))
+    return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_tuned: null scale");
+  if (group_m < 0) return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_tuned: group_m < 0");
+  if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
+  return fp8 ? dispatch_gemm<true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, stages, group_m,
+                                   epilogue, status, stream)
+             : dispatch_gemm<false>(A, B, C, M, N, K, nullptr, nullptr, cta_group, stages,
+                                    group_m, epilogue, status, stream);
 }
 
 extern "C" int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
@@ -375,9 +486,8 @@ extern "C" int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int 
   if (scale_a == nullptr || scale_b == nullptr)
     return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_e4m3: null scale");
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
-  return cta_group == 1
-             ? launch_gemm<1, true>(A, B, C, M, N, K, scale_a, scale_b, status, stream)
-             : launch_gemm<2, true>(A, B, C, M, N, K, scale_a, scale_b, status, stream);
+  return dispatch_gemm<true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, 0, 0, 0, status,
+                             stream);
 }
 
 extern "C" int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst,

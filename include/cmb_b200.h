@@ -188,6 +188,24 @@ int cmb_gemm_bf16(const void *A, const void *B, float *C, int M, int N, int K, i
 int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
                   const float *scale_a, const float *scale_b, int cta_group, int *status,
                   cmb_stream_t stream);
+/* cmb_gemm_bf16 (fp8 = 0) or cmb_gemm_e4m3 (fp8 = 1) with an explicit
+ * pipeline shape, for sweeps: stages 3-4 (cta_group 1) or 4-6 (cta_group 2;
+ * 7 with epilogue 1), 0 = default (4); group_m = tile rows per raster
+ * group, 0 = default (8); epilogue 1 = direct stores, 2 = TMA stores (needs
+ * N % 4 == 0), 0 = default (2 when possible). */
+int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int N, int K, int fp8,
+                   const float *scale_a, const float *scale_b, int cta_group, int stages,
+                   int group_m, int epilogue, int *status, cmb_stream_t stream);
+/* Tensor-pipe ceiling: `ctas` CTAs (one per SM) each issue `iters` rounds of
+ * four tcgen05.mma M=128 N=256 (bf16: fp8 = 0, K = 16; e4m3: fp8 = 1,
+ * K = 32) on all-ones operands resident in shared memory, into TMEM, with no
+ * other memory traffic.  out (device, ctas * 128 floats) = one accumulator
+ * value per row, each iters * 4 * K (status CMB_ERR_MISMATCH if any checked
+ * element differs); cycles (device, ctas x uint64, may be NULL) = SM cycles
+ * of each CTA's issue loop.  The tcgen05 counterpart of the register-only
+ * mma.sync throughput kernels (src/tensor_core_extended.cu:170-250). */
+int cmb_mma_rate(int fp8, int iters, int ctas, float *out, uint64_t *cycles, int *status,
+                 cmb_stream_t stream);
 /* Per-tensor e4m3 quantisation of n bf16 values: amax = max |x|,
  * dst[i] = e4m3_satfinite(x[i] * (448 / amax)) (fp32 multiply, round to
  * nearest even), scale_out[0] = amax / 448 (the dequantisation factor),

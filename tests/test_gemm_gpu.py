@@ -51,7 +51,7 @@ def _check_tiles(orc, A_h, B_h, C, K, tiles, dtype=0, sa=1.0, sb=1.0):
 
 @pytest.mark.parametrize("cg", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (256, 512, 1024), (200, 136, 72),
-                                   (1000, 700, 520), (128, 256, 8)])
+                                   (1000, 700, 520), (128, 256, 8), (96, 130, 64)])
 def test_gemm_bf16_small_full_check(cuda, cmb, orc, cg, M, N, K):
     A = _normal_bf16(cuda, cmb, M, K, 1, K ** -0.5)
     B = _normal_bf16(cuda, cmb, N, K, 2, K ** -0.5)
@@ -125,6 +125,48 @@ def test_gemm_e4m3(cuda, cmb, orc, cg, M, N, K):
     _check_tiles(orc, qa_h, qb_h, C, K, tiles, dtype=1, sa=sa_h, sb=sb_h)
 
 
+@pytest.mark.parametrize("fp8", [0, 1])
+@pytest.mark.parametrize("cg,stages,epi", [(1, 3, 1), (1, 4, 2), (2, 4, 1), (2, 5, 2), (2, 6, 2),
+                                           (2, 7, 1)])
+def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi):
+    M, N, K = 700, 520, 1040
+    A = _normal_bf16(cuda, cmb, M, K, 31, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 32, K ** -0.5)
+    C = cuda.full((M * N,), float("nan"), dtype=cuda.float32, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    if fp8:
+        qa, sa = _quantize(cuda, cmb, A)
+        qb, sb = _quantize(cuda, cmb, B)
+        cmb.check("cmb_gemm_tuned", dptr(qa), dptr(qb), dptr(C), M, N, K, 1, dptr(sa), dptr(sb), cg,
+                  stages, 4, epi, dptr(status), stream_handle(cuda))
+        a_h, b_h, dt = qa.cpu().numpy(), qb.cpu().numpy(), 1
+        s_a, s_b = float(sa[0].item()), float(sb[0].item())
+    else:
+        cmb.check("cmb_gemm_tuned", dptr(A), dptr(B), dptr(C), M, N, K, 0, None, None, cg, stages,
+                  4, epi, dptr(status), stream_handle(cuda))
+        a_h, b_h, dt = A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16), 0
+        s_a = s_b = 1.0
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    _check_tiles(orc, a_h, b_h, C.cpu().numpy().reshape(M, N), K, [(0, 0, M, N)], dtype=dt,
+                 sa=s_a, sb=s_b)
+
+
+@pytest.mark.parametrize("fp8", [0, 1])
+def test_mma_rate_constant_operands(cuda, cmb, fp8):
+    ctas, iters = 8, 1000
+    out = cuda.zeros(ctas * 128, dtype=cuda.float32, device="cuda")
+    cyc = cuda.zeros(ctas, dtype=cuda.int64, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    cmb.check("cmb_mma_rate", fp8, iters, ctas, dptr(out), dptr(cyc), dptr(status),
+              stream_handle(cuda))
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    # ones x ones: each MMA adds K (16 bf16 / 32 e4m3) to every element
+    assert bool((out == iters * 4 * (32 if fp8 else 16)).all())
+    assert int(cyc.min()) > 0
+
+
 def test_gemm_rejects_bad_args(cuda, cmb):
     a = cuda.zeros(1024, dtype=cuda.int16, device="cuda")
     c = cuda.zeros(1024, dtype=cuda.float32, device="cuda")
@@ -134,3 +176,8 @@ def test_gemm_rejects_bad_args(cuda, cmb):
     assert cmb.lib.cmb_gemm_bf16(dptr(a), dptr(a), dptr(c), 0, 16, 16, 1, None, s) == 1
     assert cmb.lib.cmb_gemm_e4m3(dptr(a), dptr(a), dptr(c), 16, 16, 16, None, None, 1, None,
                                  s) == 1
+    # TMA-store epilogue needs N % 4 == 0; 7 stages only with direct stores
+    assert cmb.lib.cmb_gemm_tuned(dptr(a), dptr(a), dptr(c), 16, 18, 16, 0, None, None, 2, 4, 0, 2,
+                                  None, s) == 1
+    assert cmb.lib.cmb_gemm_tuned(dptr(a), dptr(a), dptr(c), 16, 16, 16, 0, None, None, 2, 7, 0, 2,
+                                  None, s) == 1
