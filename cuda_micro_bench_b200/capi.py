@@ -48,6 +48,17 @@ SIGNATURES = {
     "cmb_gemm_tuned": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _i, _i, _i, _i, _p, _p]),
     "cmb_mma_rate": (_i, [_i, _i, _i, _p, _p, _p, _p]),
     "cmb_quantize_e4m3": (_i, [_p, _sz, _p, _p, _p]),
+    "cmb_mma_sync_latency": (_i, [_i, _i, _p, _p, _p]),
+    "cmb_mma_sync_throughput": (_i, [_i, _i, _i, _i, _p, _p]),
+    "cmb_compare_bytes": (_i, [_p, _p, _sz, _p, _p]),
+    "cmb_benchmark_global_memory": (_i, []),
+    "cmb_benchmark_cache": (_i, []),
+    "cmb_benchmark_tma": (_i, []),
+    "cmb_benchmark_tensor_core": (_i, []),
+    "cmb_benchmark_tensor_core_extended": (_i, []),
+    "cmb_benchmark_multi_gpu": (_i, []),
+    "cmb_results_log_report_placeholders": (_i, []),
+    "cmb_run_cli": (_i, [_i, _p, _s]),
     "cmb_results_set_device": (_i, [_s, _s, _i, _i, _i, _i]),
     "cmb_results_log": (_i, [_s, _s, _d, _s]),
     "cmb_results_write_json": (_i, [_s]),

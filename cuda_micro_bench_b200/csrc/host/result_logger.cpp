@@ -34,6 +34,12 @@ bool ResultLogger::hasDevice() const {
   return !device_.empty();
 }
 
+bool ResultLogger::has(const std::string &section, const std::string &key) const {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto it = sections_.find(section);
+  return it != sections_.end() && it->second.count(key) != 0;
+}
+
 void ResultLogger::clear() {
   std::lock_guard<std::mutex> lock(mu_);
   device_.clear();

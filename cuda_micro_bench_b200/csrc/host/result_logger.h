@@ -21,6 +21,7 @@ class ResultLogger {
   void log(const std::string &section, const std::string &key, double value,
            const std::string &unit = "");
   bool hasDevice() const;
+  bool has(const std::string &section, const std::string &key) const;
   // Serialised table (the exact bytes writeJson stores).
   std::string toJson() const;
   // Returns false (and leaves the reason in `err`) if the file cannot be

@@ -1,0 +1,688 @@
+// sections.cpp — the probe sections (see sections.h) and the CLI.
+#include "sections.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../../include/cmb_b200.h"
+#include "../cmb_host.h"
+#include "result_logger.h"
+
+namespace cmb {
+namespace {
+
+#define TRY(expr)                   \
+  do {                              \
+    const int rc_ = (expr);         \
+    if (rc_ != CMB_OK) return rc_;  \
+  } while (0)
+
+constexpr uint64_t kStreamSeed = 0x5EED, kChaseSeed = 0xC0DA, kGemmSeed = 0x6E33;
+
+// Device buffer owned by a section (each section frees what it allocates,
+// as the reference's sections do).
+struct DevBuf {
+  void *p = nullptr;
+  DevBuf() = default;
+  DevBuf(const DevBuf &) = delete;
+  ~DevBuf() {
+    if (p != nullptr) cudaFree(p);
+  }
+  int alloc(size_t bytes) {
+    CMB_CUDA_TRY(cudaMalloc(&p, bytes == 0 ? 1 : bytes));
+    return CMB_OK;
+  }
+  template <class T>
+  T *as() const {
+    return static_cast<T *>(p);
+  }
+};
+
+// Milliseconds of each of `runs` launches of fn (CUDA events on the legacy
+// default stream); returns the median after dropping the first `drop`
+// (src/mem_global.cu:42-53 drops one of six and takes the median of five).
+template <class F>
+int time_median(F fn, int runs, int drop, double *ms_out) {
+  cudaEvent_t a, b;
+  CMB_CUDA_TRY(cudaEventCreate(&a));
+  CMB_CUDA_TRY(cudaEventCreate(&b));
+  std::vector<double> ms;
+  for (int r = 0; r < runs; ++r) {
+    CMB_CUDA_TRY(cudaEventRecord(a, nullptr));
+    const int rc = fn();
+    if (rc != CMB_OK) return rc;
+    CMB_CUDA_TRY(cudaEventRecord(b, nullptr));
+    CMB_CUDA_TRY(cudaEventSynchronize(b));
+    float t = 0.f;
+    CMB_CUDA_TRY(cudaEventElapsedTime(&t, a, b));
+    if (r >= drop) ms.push_back(t);
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  std::sort(ms.begin(), ms.end());
+  *ms_out = ms[ms.size() / 2];
+  return CMB_OK;
+}
+
+double gib_per_s(double bytes, double ms) { return bytes / (ms * 1e-3) / (1024.0 * 1024.0 * 1024.0); }
+double gb_per_s(double bytes, double ms) { return bytes / (ms * 1e-3) / 1e9; }
+double nominal_ns(double cycles, int clock_khz) { return cycles * 1e6 / clock_khz; }
+
+unsigned host_threads() {
+  unsigned n = std::thread::hardware_concurrency();
+  return n == 0 ? 1 : std::min(n, 64u);
+}
+
+// fp64 sum of the uniform stream cmb_fill_uniform_f32 writes (the same
+// SplitMix64 formula, regenerated on the host).
+double host_uniform_sum(size_t n, uint64_t seed) {
+  const unsigned nt = host_threads();
+  std::vector<double> part(nt, 0.0);
+  std::vector<std::thread> pool;
+  for (unsigned t = 0; t < nt; ++t)
+    pool.emplace_back([&, t] {
+      double s = 0.0;
+      for (size_t i = n * t / nt; i < n * (t + 1) / nt; ++i) {
+        uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        s += static_cast<double>(static_cast<float>(static_cast<uint32_t>(z >> 40)) * 0x1p-23f - 1.0f);
+      }
+      part[t] = s;
+    });
+  for (auto &th : pool) th.join();
+  double s = 0.0;
+  for (double v : part) s += v;
+  return s;
+}
+
+int expect_equal(const void *a, const void *b, size_t bytes, bool *equal) {
+  DevBuf cnt;
+  TRY(cnt.alloc(sizeof(unsigned long long)));
+  TRY(cmb_compare_bytes(a, b, bytes, cnt.as<unsigned long long>(), nullptr));
+  unsigned long long h = 1;
+  CMB_CUDA_TRY(cudaMemcpy(&h, cnt.p, sizeof(h), cudaMemcpyDeviceToHost));
+  *equal = (h == 0);
+  return CMB_OK;
+}
+
+// ------------------------------------------------------------ chase
+
+struct ChaseResult {
+  double cycles_per_hop, ns_per_hop;
+};
+
+// Dependent-load chase over `bytes` (include/memory_chase.h:11-59): the link
+// array is built on the host, the endpoint is checked against a host walk
+// (failure = CMB_ERR_MISMATCH), median of five samples.
+int measure_chase(size_t bytes, bool bypass_l1, bool resident, ChaseResult *res) {
+  const size_t words = bytes / 4, slots = bytes / 128;
+  std::vector<uint32_t> links(words);
+  TRY(cmb_chase_build_links(links.data(), bytes, kChaseSeed));
+  // resident: warm the cycle twice, then 2^17 timed hops (the reference's
+  // cache probes); cold: 1024 warm-up hops, then 2^24 hops (4 walks of the
+  // 512 MiB cycle, the DRAM configuration).
+  const uint64_t warmup = resident ? 2 * slots : 1024;
+  const uint64_t hops = resident ? (1u << 17) : (1u << 24);
+  uint32_t expect = 0;
+  TRY(cmb_chase_host_walk(links.data(), words, warmup + hops, &expect));
+  DevBuf d, out;
+  TRY(d.alloc(bytes));
+  TRY(out.alloc(4 * sizeof(uint64_t)));
+  CMB_CUDA_TRY(cudaMemcpy(d.p, links.data(), bytes, cudaMemcpyHostToDevice));
+  std::vector<double> cyc, ns;
+  for (int s = 0; s < 5; ++s) {
+    TRY(cmb_chase_run(d.as<uint32_t>(), words, warmup, hops, bypass_l1 ? 1 : 0, out.as<uint64_t>(),
+                      nullptr));
+    uint64_t h[4];
+    CMB_CUDA_TRY(cudaMemcpy(h, out.p, sizeof(h), cudaMemcpyDeviceToHost));
+    if (h[3] != 0) return fail(CMB_ERR_INVALID_ARG, "pointer chase: link array rejected");
+    if (h[1] != expect)
+      return fail(CMB_ERR_MISMATCH, "Pointer chase result mismatch (%llu != %u)",
+                  static_cast<unsigned long long>(h[1]), expect);
+    cyc.push_back(static_cast<double>(h[0]) / hops);
+    ns.push_back(static_cast<double>(h[2]) / hops);
+  }
+  std::sort(cyc.begin(), cyc.end());
+  std::sort(ns.begin(), ns.end());
+  res->cycles_per_hop = cyc[2];
+  res->ns_per_hop = ns[2];
+  return CMB_OK;
+}
+
+// ------------------------------------------------------------ GEMM check
+
+float bf16_bits_to_float(uint16_t v) {
+  uint32_t u = static_cast<uint32_t>(v) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+float e4m3_to_float(uint8_t v) {
+  __nv_fp8_e4m3 x;
+  x.__x = v;
+  return static_cast<float>(x);
+}
+
+// Max over `tiles` sampled 64x64 tiles of max|C - C_fp64| / max|C_fp64|.
+template <bool kFp8>
+double sampled_gemm_error(const std::vector<uint8_t> &A, const std::vector<uint8_t> &B,
+                          const std::vector<float> &C, int M, int N, int K, double sa, double sb,
+                          int tiles) {
+  double worst = 0.0;
+  uint64_t r = 12345;
+  std::vector<double> a(64 * (size_t)K), b(64 * (size_t)K);
+  for (int t = 0; t < tiles; ++t) {
+    r = r * 6364136223846793005ull + 1442695040888963407ull;
+    const int r0 = static_cast<int>((r >> 33) % (M / 64)) * 64;
+    const int c0 = static_cast<int>((r >> 13) % (N / 64)) * 64;
+    for (int i = 0; i < 64; ++i)
+      for (int k = 0; k < K; ++k) {
+        const size_t ia = (size_t)(r0 + i) * K + k, ib = (size_t)(c0 + i) * K + k;
+        if (kFp8) {
+          a[(size_t)i * K + k] = e4m3_to_float(A[ia]) * sa;
+          b[(size_t)i * K + k] = e4m3_to_float(B[ib]) * sb;
+        } else {
+          uint16_t va, vb;
+          std::memcpy(&va, &A[2 * ia], 2);
+          std::memcpy(&vb, &B[2 * ib], 2);
+          a[(size_t)i * K + k] = bf16_bits_to_float(va);
+          b[(size_t)i * K + k] = bf16_bits_to_float(vb);
+        }
+      }
+    double ref_max = 0.0, err_max = 0.0;
+    for (int i = 0; i < 64; ++i)
+      for (int j = 0; j < 64; ++j) {
+        double s = 0.0;
+        for (int k = 0; k < K; ++k) s += a[(size_t)i * K + k] * b[(size_t)j * K + k];
+        ref_max = std::max(ref_max, std::fabs(s));
+        err_max = std::max(err_max, std::fabs(C[(size_t)(r0 + i) * N + c0 + j] - s));
+      }
+    worst = std::max(worst, err_max / std::max(ref_max, 1e-300));
+  }
+  return worst;
+}
+
+}  // namespace
+
+int query_device(int dev, DeviceInfo *info) {
+  CMB_CUDA_TRY(cudaSetDevice(dev));
+  cudaDeviceProp prop;
+  CMB_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+  info->id = dev;
+  info->name = prop.name;
+  info->cc_major = prop.major;
+  info->cc_minor = prop.minor;
+  info->sm_count = prop.multiProcessorCount;
+  info->max_threads_per_sm = prop.maxThreadsPerMultiProcessor;
+  info->max_warps_per_sm = prop.maxThreadsPerMultiProcessor / prop.warpSize;
+  CMB_CUDA_TRY(cudaDeviceGetAttribute(&info->clock_rate_khz, cudaDevAttrClockRate, dev));
+  CMB_CUDA_TRY(cudaDeviceGetAttribute(&info->memory_clock_khz, cudaDevAttrMemoryClockRate, dev));
+  info->mem_bus_width = prop.memoryBusWidth;
+  info->l2_cache_size = prop.l2CacheSize;
+  info->total_global_mem = prop.totalGlobalMem;
+  info->shared_mem_per_block_optin = prop.sharedMemPerBlockOptin;
+  g_results.setDevice(info->name, std::to_string(info->cc_major) + "." + std::to_string(info->cc_minor),
+                      info->sm_count, info->clock_rate_khz, info->memory_clock_khz,
+                      info->mem_bus_width);
+  return CMB_OK;
+}
+
+// --device: the device header and derived peaks (src/device_info.cu:6-59).
+int benchmark_device_info() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== Device Info ===\n  %s, cc %d.%d, %d SMs, %.2f GiB, L2 %d KiB, clock %.3f GHz\n",
+         info.name.c_str(), info.cc_major, info.cc_minor, info.sm_count,
+         info.total_global_mem / 1073741824.0, info.l2_cache_size / 1024,
+         info.clock_rate_khz / 1e6);
+  const double fp32 = (double)info.sm_count * 128 * 2 * info.clock_rate_khz / 1e9;
+  const double mem_bw = (double)info.memory_clock_khz * 2 * info.mem_bus_width / 8.0 / 1e6;
+  g_results.log("topology", "sm_count", info.sm_count, "");
+  g_results.log("topology", "max_warps_per_sm", info.max_warps_per_sm, "");
+  g_results.log("topology", "max_threads_per_sm", info.max_threads_per_sm, "");
+  g_results.log("topology", "l2_cache_size_mb", info.l2_cache_size / (1024.0 * 1024.0), "MiB");
+  g_results.log("topology", "shared_memory_per_block_optin_kb",
+                info.shared_mem_per_block_optin / 1024.0, "KiB");
+  g_results.log("clock", "core_clock_mhz", info.clock_rate_khz / 1000.0, "MHz");
+  g_results.log("clock", "memory_clock_mhz", info.memory_clock_khz / 1000.0, "MHz");
+  g_results.log("peak", "fp32_tflops", fp32, "TFLOP/s");
+  g_results.log("peak", "memory_bw_theoretical_gbps", mem_bw, "GB/s");
+  return CMB_OK;
+}
+
+int benchmark_global_memory() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== Global Memory Benchmarks (median of 5) ===\n");
+  const size_t sizes[] = {16ull << 20, 64ull << 20, 256ull << 20, 1ull << 30};
+  double read_gib = 0, copy_gib = 0, read_gbs = 0, copy_gbs = 0, rel_err = 0;
+  size_t reported = 0;
+  bool copy_ok = true;
+  for (size_t bytes : sizes) {
+    if (bytes > info.total_global_mem / 4) continue;
+    const size_t n = bytes / 4;
+    DevBuf a, b, sum, ws;
+    const size_t ws_bytes = cmb_stream_sum_workspace_bytes(n);
+    TRY(a.alloc(bytes));
+    TRY(b.alloc(bytes));
+    TRY(sum.alloc(sizeof(double)));
+    TRY(ws.alloc(ws_bytes));
+    TRY(cmb_fill_uniform_f32(a.as<float>(), n, kStreamSeed, nullptr));
+    double cms = 0, rms = 0;
+    TRY(time_median([&] { return cmb_stream_copy(b.p, a.p, bytes, nullptr); }, 6, 1, &cms));
+    bool eq = false;
+    TRY(expect_equal(a.p, b.p, bytes, &eq));
+    copy_ok = copy_ok && eq;
+    TRY(time_median(
+        [&] {
+          return cmb_stream_sum_f32(a.as<float>(), n, sum.as<double>(), ws.p, ws_bytes, nullptr);
+        },
+        6, 1, &rms));
+    double got = 0;
+    CMB_CUDA_TRY(cudaMemcpy(&got, sum.p, sizeof(got), cudaMemcpyDeviceToHost));
+    const double ref = host_uniform_sum(n, kStreamSeed);
+    rel_err = std::fabs(got - ref) / std::max(std::fabs(ref), 1e-300);
+    copy_gib = gib_per_s(2.0 * bytes, cms);
+    read_gib = gib_per_s((double)bytes, rms);
+    copy_gbs = gb_per_s(2.0 * bytes, cms);
+    read_gbs = gb_per_s((double)bytes, rms);
+    reported = bytes;
+    printf("  %5zu MiB: copy %.2f GiB/s (read+write, %s), read %.2f GiB/s (sum rel err %.1e)\n",
+           bytes >> 20, copy_gib, eq ? "bit-exact" : "MISMATCH", read_gib, rel_err);
+    if (!eq) return fail(CMB_ERR_MISMATCH, "stream copy output differs from its input");
+    if (rel_err > 1e-5) return fail(CMB_ERR_MISMATCH, "stream sum rel err %.3g > 1e-5", rel_err);
+  }
+  g_results.log("memory_dram", "read_bw_gibps", read_gib, "GiB/s");
+  g_results.log("memory_dram", "copy_max_bw_gibps", copy_gib, "GiB/s");
+  g_results.log("memory", "dram_read_bw_gbps", read_gib * 1.073741824, "GB/s");
+  g_results.log("memory_dram", "stream_working_set_bytes", (double)reported, "bytes");
+  g_results.log("memory_dram", "copy_bw_gbps", copy_gbs, "GB/s");
+  g_results.log("memory_dram", "copy_frac_of_8tbs_spec", copy_gbs / 8000.0, "");
+  g_results.log("memory_dram", "read_frac_of_8tbs_spec", read_gbs / 8000.0, "");
+  g_results.log("memory_dram", "copy_verified", copy_ok ? 1.0 : 0.0, "bool");
+  g_results.log("memory_dram", "read_sum_rel_err", rel_err, "");
+
+  // DRAM latency: 512 MiB link array (well above the 126 MB L2), .cg loads.
+  const size_t bytes = std::min<size_t>(512ull << 20, info.total_global_mem / 8);
+  ChaseResult cr;
+  TRY(measure_chase(bytes, true, false, &cr));
+  const double ns = nominal_ns(cr.cycles_per_hop, info.clock_rate_khz);
+  printf("  DRAM random chase (.cg, %zu MiB, 2^24 hops): %.2f cycles (%.2f nominal ns, %.2f ns "
+         "measured)\n", bytes >> 20, cr.cycles_per_hop, ns, cr.ns_per_hop);
+  g_results.log("memory", "dram_latency_cyc", cr.cycles_per_hop, "cycles");
+  g_results.log("memory_dram", "pointer_chase_latency_ns", ns, "nominal ns");
+  g_results.log("memory_dram", "pointer_chase_latency_ns_measured", cr.ns_per_hop, "ns");
+  g_results.log("memory_dram", "chase_working_set_bytes", (double)bytes, "bytes");
+  g_results.log("memory_dram", "chase_loads_per_sample", (double)(1u << 24), "loads");
+  g_results.log("memory_dram", "chase_min_sector_footprint_bytes", (double)(bytes / 4), "bytes");
+  g_results.log("memory_dram", "chase_endpoint_verified", 1.0, "bool");
+  return CMB_OK;
+}
+
+int benchmark_cache() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== Cache Benchmarks (random dependent loads, median of 5) ===\n");
+  for (int kb = 4; kb <= 256; kb *= 2) {
+    ChaseResult cr;
+    TRY(measure_chase((size_t)kb * 1024, false, true, &cr));
+    printf("    %4d KiB -> %.2f cycles/access\n", kb, cr.cycles_per_hop);
+    char key[64];
+    snprintf(key, sizeof(key), "l1_chase_%d_kb_cycles", kb);
+    g_results.log("memory_cache", key, cr.cycles_per_hop, "cycles/access");
+    if (kb == 4) g_results.log("memory", "l1_latency_cyc", cr.cycles_per_hop, "cycles");
+  }
+  const size_t l2_bytes = std::min<size_t>(8ull << 20, (size_t)info.l2_cache_size / 4);
+  if (l2_bytes >= (1ull << 20)) {
+    ChaseResult cr;
+    TRY(measure_chase(l2_bytes, true, true, &cr));
+    printf("  L2 (.cg, %zu KiB): %.2f cycles/access\n", l2_bytes / 1024, cr.cycles_per_hop);
+    g_results.log("memory", "l2_latency_cyc", cr.cycles_per_hop, "cycles");
+    g_results.log("memory_cache", "l2_chase_working_set_bytes", (double)l2_bytes, "bytes");
+  }
+  return CMB_OK;
+}
+
+int benchmark_tma() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== TMA (cp.async.bulk.tensor) Probes ===\n");
+  if (info.cc_major < 10) {
+    // The B200 kernels are sm_100a code.
+    g_results.log("tma", "tma_1d_load_latency_cyc", 0.0, "N/A");
+    g_results.log("tma", "tma_g2s_load_bw_gibps", 0.0, "N/A");
+    return fail(CMB_ERR_UNSUPPORTED, "TMA probes need an sm_100 device");
+  }
+  {
+    DevBuf buf, cyc, st;
+    TRY(buf.alloc(1024));
+    TRY(cyc.alloc(sizeof(uint32_t)));
+    TRY(st.alloc(sizeof(int)));
+    CMB_CUDA_TRY(cudaMemset(buf.p, 0, 1024));
+    const int iters = 256;
+    TRY(cmb_tma_1d_latency(buf.p, 1024, iters, cyc.as<uint32_t>(), st.as<int>(), nullptr));
+    uint32_t h = 0;
+    int status = 0;
+    CMB_CUDA_TRY(cudaMemcpy(&h, cyc.p, sizeof(h), cudaMemcpyDeviceToHost));
+    CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status != 0) return fail(status, "TMA 1-D latency: a bounded wait expired");
+    printf("  TMA 1D 16-byte load issue/wait cost: %.2f cycles\n", (double)h / iters);
+    g_results.log("tma", "tma_1d_load_latency_cyc", (double)h / iters, "cycles");
+  }
+  // 16384 x 16384 bf16, 128 x 128 boxes, 4-stage ring.
+  const int n = 16384;
+  const size_t bytes = (size_t)n * n * 2;
+  DevBuf src, dst, xo, st;
+  TRY(src.alloc(bytes));
+  TRY(dst.alloc(bytes));
+  TRY(xo.alloc(4096 * sizeof(uint32_t)));
+  TRY(st.alloc(sizeof(int)));
+  TRY(cmb_fill_normal_bf16(src.as<uint16_t>(), (size_t)n * n, kStreamSeed, 1.0f, nullptr));
+  double lms = 0, cms = 0;
+  TRY(time_median(
+      [&] {
+        return cmb_tma_tile_load_bf16(src.p, n, n, 128, 128, 4, xo.as<uint32_t>(), 4096,
+                                      st.as<int>(), nullptr);
+      },
+      6, 1, &lms));
+  TRY(time_median(
+      [&] {
+        return cmb_tma_tile_copy_bf16(dst.p, src.p, n, n, 128, 128, 4, 1, st.as<int>(), nullptr);
+      },
+      6, 1, &cms));
+  int status = 0;
+  CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+  if (status != 0) return fail(status, "TMA tile probe: a bounded wait expired");
+  bool eq = false;
+  TRY(expect_equal(src.p, dst.p, bytes, &eq));
+  if (!eq) return fail(CMB_ERR_MISMATCH, "TMA tile copy output differs from its input");
+  const double g2s = gib_per_s((double)bytes, lms);
+  printf("  TMA G2S tile load BW: %.2f GiB/s; tile copy %.2f GB/s (read+write, bit-exact)\n", g2s,
+         gb_per_s(2.0 * bytes, cms));
+  g_results.log("tma", "tma_g2s_load_bw_gibps", g2s, "GiB/s");
+  g_results.log("tma", "tile_copy_bw_gbps", gb_per_s(2.0 * bytes, cms), "GB/s");
+  g_results.log("tma", "tile_copy_frac_of_8tbs_spec", gb_per_s(2.0 * bytes, cms) / 8000.0, "");
+  g_results.log("tma", "tile_copy_verified", 1.0, "bool");
+  g_results.log("tma", "tile_box_rows", 128, "");
+  g_results.log("tma", "tile_box_cols", 128, "");
+  g_results.log("tma", "tile_stages", 4, "");
+  return CMB_OK;
+}
+
+namespace {
+
+// Legacy mma.sync latency (one warp) and throughput, logged under `section`
+// with the reference's key names.
+int mma_sync_probe(const DeviceInfo &info, int kind, const char *section, const char *label,
+                   double ops_per_mma, int k, bool int_ops, double *rate_out) {
+  const int iters = 4096;
+  DevBuf cyc, val;
+  TRY(cyc.alloc(sizeof(uint64_t)));
+  TRY(val.alloc(sizeof(double) * (size_t)info.sm_count * 4 * 8));
+  TRY(cmb_mma_sync_latency(kind, iters, cyc.as<uint64_t>(), val.as<double>(), nullptr));
+  uint64_t c = 0;
+  CMB_CUDA_TRY(cudaMemcpy(&c, cyc.p, sizeof(c), cudaMemcpyDeviceToHost));
+  const double lat = (double)c / iters;
+  const int blocks = info.sm_count * 4, warps = 8;
+  double ms = 0;
+  TRY(time_median([&] { return cmb_mma_sync_throughput(kind, iters, blocks, warps, val.as<double>(), nullptr); },
+                  3, 1, &ms));
+  double v = 0;
+  CMB_CUDA_TRY(cudaMemcpy(&v, val.p, sizeof(v), cudaMemcpyDeviceToHost));
+  // four independent chains of `iters` MMAs, each adding k per MMA (the
+  // f16 accumulator saturates, so it is not checked)
+  const bool checked = kind != 1;
+  if (checked && v != 4.0 * k * iters)
+    return fail(CMB_ERR_MISMATCH, "%s: accumulator %.1f != %.1f", label, v, 4.0 * k * iters);
+  const double ops = (double)blocks * warps * iters * 4 * ops_per_mma;
+  const double rate = ops / (ms * 1e-3) / 1e12;
+  printf("  %-18s latency %.2f cycles, throughput %.2f %s\n", label, lat, rate,
+         int_ops ? "TOP/s" : "TFLOP/s");
+  const std::string l(label), s(section);
+  if (s == "tensor_core") {
+    g_results.log(s, l + "_latency_cyc", lat, "cycles");
+    g_results.log(s, l + "_latency_ns", nominal_ns(lat, info.clock_rate_khz), "nominal ns");
+    g_results.log(s, l + "_throughput_tflops", rate, "TFLOP/s");
+  } else {
+    g_results.log(s, l + "_latency_cycles", lat, "cycles");
+    g_results.log(s, l + "_latency_ns", nominal_ns(lat, info.clock_rate_khz), "ns");
+    g_results.log(s, l + (int_ops ? "_throughput_Tops" : "_throughput_TFs"), rate,
+                  int_ops ? "TOP/s" : "TFLOP/s");
+  }
+  if (rate_out != nullptr) *rate_out = rate;
+  return CMB_OK;
+}
+
+}  // namespace
+
+int benchmark_tensor_core() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== Tensor Core Benchmarks ===\n");
+  double tf32 = 0;
+  TRY(mma_sync_probe(info, 0, "tensor_core", "mma_m16n8k8", 2.0 * 16 * 8 * 8, 8, false, &tf32));
+  // the reference records its mma.sync TF32 rate as the TF32 peak
+  // (src/tensor_core.cu:116-117)
+  g_results.log("peak", "tf32_tensor_tflops", tf32, "TFLOP/s");
+  // tcgen05 ceiling with resident shared-memory operands.
+  DevBuf out, st;
+  TRY(out.alloc((size_t)info.sm_count * 128 * sizeof(float)));
+  TRY(st.alloc(sizeof(int)));
+  for (int fp8 = 0; fp8 < 2; ++fp8) {
+    const int iters = 8192;
+    double ms = 0;
+    TRY(time_median(
+        [&] { return cmb_mma_rate(fp8, iters, info.sm_count, out.as<float>(), nullptr, st.as<int>(), nullptr); },
+        4, 1, &ms));
+    int status = 0;
+    CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status != 0) return fail(status, "tcgen05 issue-rate probe failed its check");
+    const double flop = (double)info.sm_count * iters * 4 * 2.0 * 128 * 256 * (fp8 ? 32 : 16);
+    const double tf = flop / (ms * 1e-3) / 1e12;
+    printf("  tcgen05 %s M=128 N=256 issue rate: %.1f TFLOP/s\n", fp8 ? "e4m3" : "bf16", tf);
+    g_results.log("tensor_core_tcgen05", fp8 ? "fp8_issue_rate_tflops" : "bf16_issue_rate_tflops",
+                  tf, "TFLOP/s");
+  }
+  return CMB_OK;
+}
+
+int benchmark_tensor_core_extended() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== Tensor Core Extended ===\n");
+  double fp16_tf = 0;
+  TRY(mma_sync_probe(info, 1, "tensor_core_extended", "fp16_m16n8k16", 2.0 * 16 * 8 * 16, 16, false, &fp16_tf));
+  TRY(mma_sync_probe(info, 2, "tensor_core_extended", "bf16_m16n8k16", 2.0 * 16 * 8 * 16, 16, false, nullptr));
+  TRY(mma_sync_probe(info, 3, "tensor_core_extended", "fp8_m16n8k32", 2.0 * 16 * 8 * 32, 32, false, nullptr));
+  TRY(mma_sync_probe(info, 4, "tensor_core_extended", "int8_m16n8k32", 2.0 * 16 * 8 * 32, 32, true, nullptr));
+  // the reference reports its FP16 mma.sync rate as the FP16 tensor peak
+  // (src/tensor_core_extended.cu:289-290)
+  g_results.log("peak", "fp16_tensor_tflops", fp16_tf, "TFLOP/s (FP16 accumulation)");
+
+  // tcgen05 GEMM 8192^3, BF16 and FP8 e4m3 (per-tensor scale).
+  const int M = 8192, N = 8192, K = 8192;
+  const double flop = 2.0 * M * N * K;
+  DevBuf A, B, C, qa, qb, sa, sb, st;
+  TRY(A.alloc((size_t)M * K * 2));
+  TRY(B.alloc((size_t)N * K * 2));
+  TRY(C.alloc((size_t)M * N * 4));
+  TRY(qa.alloc((size_t)M * K));
+  TRY(qb.alloc((size_t)N * K));
+  TRY(sa.alloc(2 * sizeof(float)));
+  TRY(sb.alloc(2 * sizeof(float)));
+  TRY(st.alloc(sizeof(int)));
+  const float scale = 1.0f / std::sqrt((float)K);
+  TRY(cmb_fill_normal_bf16(A.as<uint16_t>(), (size_t)M * K, kGemmSeed, scale, nullptr));
+  TRY(cmb_fill_normal_bf16(B.as<uint16_t>(), (size_t)N * K, kGemmSeed + 1, scale, nullptr));
+  TRY(cmb_quantize_e4m3(A.as<uint16_t>(), (size_t)M * K, qa.as<uint8_t>(), sa.as<float>(), nullptr));
+  TRY(cmb_quantize_e4m3(B.as<uint16_t>(), (size_t)N * K, qb.as<uint8_t>(), sb.as<float>(), nullptr));
+  std::vector<uint8_t> ha((size_t)M * K * 2), hb((size_t)N * K * 2);
+  std::vector<float> hc((size_t)M * N);
+  for (int fp8 = 0; fp8 < 2; ++fp8) {
+    double ms = 0;
+    TRY(time_median(
+        [&] {
+          return fp8 ? cmb_gemm_e4m3(qa.p, qb.p, C.as<float>(), M, N, K, sa.as<float>(), sb.as<float>(), 2,
+                                     st.as<int>(), nullptr)
+                     : cmb_gemm_bf16(A.p, B.p, C.as<float>(), M, N, K, 2, st.as<int>(), nullptr);
+        },
+        6, 1, &ms));
+    int status = 0;
+    CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status != 0) return fail(status, "tcgen05 GEMM: a bounded wait expired");
+    const size_t eb = fp8 ? 1 : 2;
+    CMB_CUDA_TRY(cudaMemcpy(ha.data(), fp8 ? qa.p : A.p, (size_t)M * K * eb, cudaMemcpyDeviceToHost));
+    CMB_CUDA_TRY(cudaMemcpy(hb.data(), fp8 ? qb.p : B.p, (size_t)N * K * eb, cudaMemcpyDeviceToHost));
+    CMB_CUDA_TRY(cudaMemcpy(hc.data(), C.p, hc.size() * 4, cudaMemcpyDeviceToHost));
+    float hs[2] = {1.f, 1.f}, hs2[2] = {1.f, 1.f};
+    if (fp8) {
+      CMB_CUDA_TRY(cudaMemcpy(hs, sa.p, sizeof(hs), cudaMemcpyDeviceToHost));
+      CMB_CUDA_TRY(cudaMemcpy(hs2, sb.p, sizeof(hs2), cudaMemcpyDeviceToHost));
+    }
+    const double err = fp8 ? sampled_gemm_error<true>(ha, hb, hc, M, N, K, hs[0], hs2[0], 8)
+                           : sampled_gemm_error<false>(ha, hb, hc, M, N, K, 1.0, 1.0, 8);
+    const double tf = flop / (ms * 1e-3) / 1e12;
+    const double spec = fp8 ? 4500.0 : 2250.0;
+    const std::string p = fp8 ? "fp8_e4m3_gemm_8192" : "bf16_gemm_8192";
+    printf("  tcgen05 %s GEMM 8192^3 (2-CTA 256x256): %.1f TFLOP/s (%.1f%% of %.0f), sampled "
+           "rel err %.1e\n", fp8 ? "e4m3" : "bf16", tf, 100 * tf / spec, spec, err);
+    if (err > 1e-2) return fail(CMB_ERR_MISMATCH, "%s: sampled rel err %.3g > 1e-2", p.c_str(), err);
+    g_results.log("tensor_core_tcgen05", p + "_tflops", tf, "TFLOP/s");
+    g_results.log("tensor_core_tcgen05", p + "_frac_of_spec", tf / spec, "");
+    g_results.log("tensor_core_tcgen05", p + "_max_rel_err", err, "");
+    g_results.log("tensor_core_tcgen05", p + "_verified", 1.0, "bool");
+  }
+  return CMB_OK;
+}
+
+int benchmark_multi_gpu() {
+  int count = 0;
+  CMB_CUDA_TRY(cudaGetDeviceCount(&count));
+  printf("=== Multi-GPU (NVLink P2P) ===\n  %d device(s)\n", count);
+  g_results.log("p2p", "device_count", count, "");
+  return CMB_OK;
+}
+
+void log_report_placeholders() {
+  static const char *const kKeys[][2] = {
+#include "report_keys.inc"
+  };
+  for (const auto &k : kKeys)
+    if (!g_results.has(k[0], k[1])) g_results.log(k[0], k[1], 0.0, "N/A");
+}
+
+namespace {
+
+struct Section {
+  const char *flag, *help;
+  int (*run)();
+};
+
+const Section kSections[] = {
+    {"--device", "Device / SM info and derived peaks", benchmark_device_info},
+    {"--memory", "HBM read/copy streams and DRAM pointer chase", benchmark_global_memory},
+    {"--cache", "L1/L2 dependent-load latency sweep", benchmark_cache},
+    {"--tma", "TMA bulk-tensor latency, tile load and tile copy", benchmark_tma},
+    {"--tensor", "mma.sync TF32 and tcgen05 issue-rate probes", benchmark_tensor_core},
+    {"--tensor-ext", "mma.sync FP16/BF16/FP8/INT8 and tcgen05 BF16/FP8 GEMM", benchmark_tensor_core_extended},
+    {"--p2p", "Multi-GPU sharded stream and NVLink peer copies", benchmark_multi_gpu},
+};
+
+void usage(const char *name) {
+  printf("Usage: %s [option]...\nOptions:\n", name);
+  for (const auto &s : kSections) printf("  %-12s %s\n", s.flag, s.help);
+  printf("  %-12s %s\n", "--json", "Run all sections and write the results file");
+  printf("  %-12s %s\n", "--all", "Run all sections (default)");
+}
+
+int run_all() {
+  for (const auto &s : kSections) {
+    const int rc = s.run();
+    if (rc != CMB_OK) return rc;
+  }
+  log_report_placeholders();
+  return CMB_OK;
+}
+
+int report_failure(int rc) {
+  fprintf(stderr, "cmb_b200: %s: %s\n", cmb_status_string(rc), cmb_last_error());
+  return 1;
+}
+
+int write_results(const char *path) {
+  std::string err;
+  if (!g_results.writeJson(path, &err)) {
+    fprintf(stderr, "%s\n", err.c_str());
+    return 1;
+  }
+  return 0;
+}
+
+}  // namespace
+
+int run_cli(int argc, const char *const *argv, const char *json_path) {
+  if (argc <= 1) {
+    const int rc = run_all();
+    if (rc != CMB_OK) return report_failure(rc);
+    return write_results(json_path);
+  }
+  bool ok = true, ran = false;
+  for (int i = 1; i < argc; ++i) {
+    const char *opt = argv[i];
+    if (std::strcmp(opt, "--help") == 0 || std::strcmp(opt, "-h") == 0) {
+      usage("cmb_b200");
+      ran = true;
+      continue;
+    }
+    int rc = -1;
+    if (std::strcmp(opt, "--all") == 0 || std::strcmp(opt, "--json") == 0) {
+      rc = run_all();
+    } else {
+      for (const auto &s : kSections)
+        if (std::strcmp(opt, s.flag) == 0) rc = s.run();
+    }
+    if (rc == -1) {
+      printf("Unknown option: %s\n", opt);
+      usage(argv[0]);
+      ok = false;
+    } else if (rc != CMB_OK) {
+      return report_failure(rc);
+    } else {
+      ran = true;
+    }
+  }
+  if (ran && ok && g_results.hasDevice()) {
+    if (write_results(json_path) != 0) return 1;
+  }
+  return ok ? 0 : 1;
+}
+
+}  // namespace cmb
+
+using namespace cmb;
+
+extern "C" int cmb_benchmark_global_memory(void) { return benchmark_global_memory(); }
+extern "C" int cmb_benchmark_cache(void) { return benchmark_cache(); }
+extern "C" int cmb_benchmark_tma(void) { return benchmark_tma(); }
+extern "C" int cmb_benchmark_tensor_core(void) { return benchmark_tensor_core(); }
+extern "C" int cmb_benchmark_tensor_core_extended(void) { return benchmark_tensor_core_extended(); }
+extern "C" int cmb_benchmark_multi_gpu(void) { return benchmark_multi_gpu(); }
+extern "C" int cmb_results_log_report_placeholders(void) {
+  log_report_placeholders();
+  return CMB_OK;
+}
+extern "C" int cmb_run_cli(int argc, const char *const *argv, const char *json_path) {
+  return run_cli(argc, argv, json_path ? json_path : "results/results.json");
+}

@@ -213,6 +213,52 @@ int cmb_mma_rate(int fp8, int iters, int ctas, float *out, uint64_t *cycles, int
 int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst, float *scale_out,
                       cmb_stream_t stream);
 
+/* --- legacy warp-level mma.sync probes (src/tensor_core.cu,
+ *     src/tensor_core_extended.cu) ------------------------------------- */
+
+/* kind: 0 = tf32 m16n8k8 (f32 acc), 1 = f16 m16n8k16 (f16 acc), 2 = bf16
+ * m16n8k16 (f32 acc), 3 = e4m3 m16n8k32 (f32 acc), 4 = s8 m16n8k32 (s32 acc);
+ * all operands 1.  Latency: one warp runs a dependent chain of `iters` MMAs;
+ * *cycles (device) = SM cycles of the chain, *value (device) = accumulator
+ * element 0 (iters * K; f16 saturates).  Replaces kernel_mma_latency and
+ * kernel_hmma_*_latency (src/tensor_core.cu:13-39,
+ * src/tensor_core_extended.cu:21-46,77-102,133-158,189-214). */
+int cmb_mma_sync_latency(int kind, int iters, uint64_t *cycles, double *value,
+                         cmb_stream_t stream);
+/* Throughput: blocks x warps_per_block warps each run four independent
+ * chains of `iters` MMAs; values (device, one double per warp) = sum of the
+ * four chains' element 0.  Replaces kernel_mma_throughput and
+ * kernel_hmma_*_throughput (src/tensor_core.cu:41-64,
+ * src/tensor_core_extended.cu:48-72,104-128,160-184,216-240). */
+int cmb_mma_sync_throughput(int kind, int iters, int blocks, int warps_per_block,
+                            double *values, cmb_stream_t stream);
+
+/* --- checks ---------------------------------------------------------- */
+
+/* *mismatches (device) = 0 iff a[0:bytes) == b[0:bytes) (otherwise the
+ * number of differing 32-bit words, or bytes when a or b is not 16-byte
+ * aligned). */
+int cmb_compare_bytes(const void *a, const void *b, size_t bytes,
+                      unsigned long long *mismatches, cmb_stream_t stream);
+
+/* --- probe sections (src/main.cu:9-32) --------------------------------
+ * Each runs one section on device 0 like the reference's
+ * `void cmb::benchmark_<section>()`: allocates, checks outputs, times, and
+ * logs into the results table under the reference's keys (plus new ones);
+ * returns a status instead of exiting. */
+int cmb_benchmark_global_memory(void);       /* src/mem_global.cu:27-75 */
+int cmb_benchmark_cache(void);               /* src/mem_cache.cu:4-24 */
+int cmb_benchmark_tma(void);                 /* src/tma.cu:157-259 */
+int cmb_benchmark_tensor_core(void);         /* src/tensor_core.cu:66-120 */
+int cmb_benchmark_tensor_core_extended(void);  /* src/tensor_core_extended.cu:321-357 */
+int cmb_benchmark_multi_gpu(void);           /* new: NVLink P2P and sharded stream */
+/* Logs "N/A" for every key the reference's results/report.html reads that
+ * no section logged, so the report renders. */
+int cmb_results_log_report_placeholders(void);
+/* The CLI (src/main.cu:156-181) with results written to json_path (NULL:
+ * results/results.json); returns the process exit code. */
+int cmb_run_cli(int argc, const char *const *argv, const char *json_path);
+
 /* --- results table (include/result_logger.h, src/result_logger.cu) --- */
 
 /* Same meaning as ResultLogger::setDevice (include/result_logger.h:113-121). */

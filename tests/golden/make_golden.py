@@ -6,6 +6,12 @@ logger_*.script / logger_*.json
     reference sources by `make -C oracle ref`, writes for them.  These pin
     cmb_results_* (the results.json writer) byte for byte.
 
+report_keys.txt
+    Every results key path the reference's HTML report reads
+    (results/report.html, the ['results', section, key] lists of its
+    tables), one "section key" per line: the CLI's full run must produce
+    each of them.
+
 Run here, where the reference tree is present:
     python tests/golden/make_golden.py
 """
@@ -50,8 +56,28 @@ SCRIPTS = {
 }
 
 
+REPORT = "/root/reference/results/report.html"
+
+
+def report_keys():
+    import re
+
+    html = open(REPORT).read()
+    pattern = re.compile(r"\[((?:\s*'[^']+'\s*,)*\s*'[^']+'\s*)\]", re.MULTILINE)
+    keys = set()
+    for m in pattern.findall(html):
+        parts = [p.strip().strip("'") for p in m.split(",") if p.strip()]
+        if len(parts) == 3 and parts[0] == "results":
+            keys.add((parts[1], parts[2]))
+    return sorted(keys)
+
+
 def main() -> None:
     import oracle
+
+    with open(os.path.join(HERE, "report_keys.txt"), "w") as f:
+        for sec, key in report_keys():
+            f.write(f"{sec} {key}\n")
 
     oracle.build(ref=True)
     for name, lines in SCRIPTS.items():

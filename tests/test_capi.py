@@ -107,3 +107,39 @@ def test_chase_host_walk_matches_oracle(cmb, orc):
     links[0] = 1 << 30  # leaves the array on the first hop
     assert cmb.lib.cmb_chase_host_walk(ctypes.c_void_p(links.ctypes.data), links.size, 5,
                                        ctypes.byref(out)) == 1
+
+
+def _report_keys():
+    return [tuple(l.split()) for l in open(os.path.join(GOLDEN, "report_keys.txt")) if l.strip()]
+
+
+def test_report_placeholders_cover_every_report_key(cmb, tmp_path):
+    import json
+
+    cmb.check("cmb_results_clear")
+    cmb.check("cmb_results_set_device", b"NVIDIA B200", b"10.0", 148, 1965000, 3996000, 8192)
+    cmb.check("cmb_results_log", b"memory", b"dram_latency_cyc", 812.0, b"cycles")
+    cmb.check("cmb_results_log_report_placeholders")
+    out = tmp_path / "r.json"
+    cmb.check("cmb_results_write_json", str(out).encode())
+    data = json.loads(out.read_text())["results"]
+    keys = _report_keys()
+    assert len(keys) == 195
+    for sec, key in keys:
+        assert key in data[sec], (sec, key)
+    # measured values are kept, the rest are null with unit N/A
+    assert data["memory"]["dram_latency_cyc"]["value"] == 812.0
+    assert data["atomics"]["block_reduce_latency_cyc"] == {"value": None, "unit": "N/A"}
+
+
+def test_cli_usage_and_unknown_flag(tmp_path):
+    import subprocess
+
+    exe = os.path.join(ROOT, "cuda_micro_bench_b200", "bin", "cmb_b200")
+    out = tmp_path / "x.json"
+    p = subprocess.run([exe, "--help", f"--out={out}"], capture_output=True, text=True)
+    assert p.returncode == 0 and "--memory" in p.stdout and "--tensor-ext" in p.stdout
+    assert not out.exists()  # no section ran, nothing to write
+    p = subprocess.run([exe, "--bogus", f"--out={out}"], capture_output=True, text=True)
+    assert p.returncode == 1 and "Unknown option: --bogus" in p.stdout
+    assert not out.exists()
