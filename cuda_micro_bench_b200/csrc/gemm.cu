@@ -262,28 +262,32 @@ __global__ void __launch_bounds__(192, 1)
           // Stage the warp's 32 x 32 box in shared memory (128-byte
           // swizzle: 16-byte chunk j of row r at (j ^ (r % 8)) * 16, which
           // also keeps the 8 lanes of each store phase on distinct banks)
-          // and write it out with one tiled TMA store.
-          uint8_t *box = epi + (size_t)(epi_count & 1) * Cfg::kEpiBoxBytes;
-          if (lane == 0) dev::bulk_wait_group_read<1>();  // the store 2 boxes ago has read it
-          __syncwarp();
-          const uint32_t rb = dev::smem_addr(box) + lane * 128;
+          // and write it out with one tiled TMA store.  Boxes wholly outside
+          // C are skipped without touching a buffer, so every buffer reuse
+          // follows the committed store that last read it.
+          if (row0 < M && col0 < N) {  // warp-uniform
+            uint8_t *box = epi + (size_t)(epi_count & 1) * Cfg::kEpiBoxBytes;
+            if (lane == 0) dev::bulk_wait_group_read<1>();  // the store 2 boxes ago has read it
+            __syncwarp();
+            const uint32_t rb = dev::smem_addr(box) + lane * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t addr = rb + ((static_cast<uint32_t>(j) ^ (lane & 7)) << 4);
-            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
-                         "f"(scale * __uint_as_float(r[4 * j])),
-                         "f"(scale * __uint_as_float(r[4 * j + 1])),
-                         "f"(scale * __uint_as_float(r[4 * j + 2])),
-                         "f"(scale * __uint_as_float(r[4 * j + 3]))
-                         : "memory");
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t addr = rb + ((static_cast<uint32_t>(j) ^ (lane & 7)) << 4);
+              asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
+                           "f"(scale * __uint_as_float(r[4 * j])),
+                           "f"(scale * __uint_as_float(r[4 * j + 1])),
+                           "f"(scale * __uint_as_float(r[4 * j + 2])),
+                           "f"(scale * __uint_as_float(r[4 * j + 3]))
+                           : "memory");
+            }
+            dev::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
+              dev::bulk_commit_group();
+            }
+            ++epi_count;
           }
-          dev::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && row0 < M && col0 < N) {
-            dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
-            dev::bulk_commit_group();
-          }
-          ++epi_count;
         } else if (row < M) {
           if (vec_ok && col0 + 32 <= N) {
 #pragma unroll

@@ -152,6 +152,26 @@ def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi):
                  sa=s_a, sb=s_b)
 
 
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("epi", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(1000, 700, 512), (1024, 700, 64), (1000, 136, 520)])
+def test_gemm_ragged_columns(cuda, cmb, orc, cg, epi, M, N, K):
+    """Column edges where the last stored box is clipped and the boxes after
+    it lie wholly outside C (the staged TMA-store epilogue must not reuse a
+    buffer a clipped store is still reading)."""
+    A = _normal_bf16(cuda, cmb, M, K, 41, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 42, K ** -0.5)
+    C = cuda.full((M * N,), float("nan"), dtype=cuda.float32, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    for _ in range(3):
+        cmb.check("cmb_gemm_tuned", dptr(A), dptr(B), dptr(C), M, N, K, 0, None, None, cg, 0, 0, epi,
+                  dptr(status), stream_handle(cuda))
+        cuda.cuda.synchronize()
+        assert int(status.item()) == 0
+        _check_tiles(orc, A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16),
+                     C.cpu().numpy().reshape(M, N), K, [(0, 0, M, N)])
+
+
 @pytest.mark.parametrize("fp8", [0, 1])
 def test_mma_rate_constant_operands(cuda, cmb, fp8):
     ctas, iters = 8, 1000
