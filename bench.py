@@ -517,6 +517,53 @@ def probe_gemm(torch, stream, sh, peaks):
     return out
 
 
+def probe_p2p(args, ranks) -> dict:
+    """Config: 256 MiB seeded random bytes per GPU exchanged over NVLink,
+    ring (-> rank+1) and all-to-all (N chunks), by in-kernel peer stores and
+    by the copy engines; bit-exact receive check.  Time = max over ranks of
+    each rank's device time (CUDA events), median of 5 repetitions."""
+    import torch
+
+    from cuda_micro_bench_b200 import multi_gpu
+
+    nbytes = 1 << 28
+    stream = torch.cuda.current_stream()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    ex = multi_gpu.PeerExchange(ranks, nbytes, SEED)
+    out = {}
+    try:
+        for mode in ("ring", "alltoall"):
+            egress = multi_gpu.egress_bytes(mode, ranks.rank, ranks.world, nbytes)
+            for method in ("store", "copy_engine"):
+                times = []
+                for rep in range(2 + 5):
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    ranks.barrier()
+                    torch.cuda.synchronize()
+                    a.record(stream)
+                    ex.launch(mode, method, sh)
+                    b.record(stream)
+                    torch.cuda.synchronize()
+                    ranks.barrier()
+                    t = ranks.max(a.elapsed_time(b))
+                    if rep >= 2:
+                        times.append(t)
+                ms = statistics.median(times)
+                bad = ranks.sum(float(ex.mismatches(mode, sh)))
+                link = egress / (ms * 1e-3) / 1e9
+                out[f"{mode}_{method}"] = {
+                    "per_gpu_egress_GB/s": round(link, 2),
+                    "aggregate_GB/s": round(ranks.world * link, 2),
+                    "frac_of_900_spec": round(link / 900.0, 4),
+                    "frac_of_770_measured_peer_copy": round(link / 770.0, 4),
+                    "ms": round(ms, 4), "egress_bytes_per_gpu": egress,
+                    "bit_exact": bad == 0}
+    finally:
+        ex.close()
+    return out
+
+
 def run_probe_only(args) -> int:
     """Runs only the named probes (for profiling) and prints their results."""
     import torch
@@ -546,6 +593,8 @@ def run_probes(args, ranks, peaks) -> dict:
     stream = torch.cuda.current_stream()
     sh = ctypes.c_void_p(stream.cuda_stream)
     out = {}
+    if ranks.world > 1:
+        out["p2p_256mib"] = probe_p2p(args, ranks)
     if ranks.world == 1:
         out.update(probe_stream_1gib(torch, stream, sh, peaks))
         out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (24 if args.full_chase else 22))

@@ -50,6 +50,15 @@ SIGNATURES = {
     "cmb_quantize_e4m3": (_i, [_p, _sz, _p, _p, _p]),
     "cmb_mma_sync_latency": (_i, [_i, _i, _p, _p, _p]),
     "cmb_mma_sync_throughput": (_i, [_i, _i, _i, _i, _p, _p]),
+    "cmb_p2p_alloc": (_i, [_sz, _p]),
+    "cmb_p2p_free": (_i, [_p]),
+    "cmb_ipc_handle_bytes": (_sz, []),
+    "cmb_ipc_get_handle": (_i, [_p, _p]),
+    "cmb_ipc_open": (_i, [_p, _p]),
+    "cmb_ipc_close": (_i, [_p]),
+    "cmb_p2p_enable_peer": (_i, [_i]),
+    "cmb_p2p_scatter_store": (_i, [_p, _p, _p, _i, _i, _p]),
+    "cmb_p2p_scatter_copy_engine": (_i, [_p, _p, _p, _i, _p]),
     "cmb_compare_bytes": (_i, [_p, _p, _sz, _p, _p]),
     "cmb_benchmark_global_memory": (_i, []),
     "cmb_benchmark_cache": (_i, []),

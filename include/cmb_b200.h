@@ -233,6 +233,37 @@ int cmb_mma_sync_latency(int kind, int iters, uint64_t *cycles, double *value,
 int cmb_mma_sync_throughput(int kind, int iters, int blocks, int warps_per_block,
                             double *values, cmb_stream_t stream);
 
+/* --- multi-GPU: NVLink peer copies (new; the reference only queries
+ *     cudaDeviceCanAccessPeer, src/pcie.cu:100-112) -------------------- */
+
+/* Device buffers that peers may map: plain cudaMalloc / cudaFree (an IPC
+ * handle must name the start of an allocation). */
+int cmb_p2p_alloc(size_t bytes, void **out);
+int cmb_p2p_free(void *ptr);
+/* Bytes of an IPC handle (64). */
+size_t cmb_ipc_handle_bytes(void);
+/* handle_out (host, cmb_ipc_handle_bytes() bytes) names the allocation that
+ * starts at `base` (from cmb_p2p_alloc), for another process to open. */
+int cmb_ipc_get_handle(void *base, void *handle_out);
+/* Maps another process's allocation into this one (peer access enabled on
+ * first use); *peer_ptr is a device pointer usable by this GPU's kernels and
+ * copy engines. */
+int cmb_ipc_open(const void *handle, void **peer_ptr);
+int cmb_ipc_close(void *peer_ptr);
+/* One process driving several GPUs: lets the current device access
+ * `peer_device`'s memory (no error if already enabled). */
+int cmb_p2p_enable_peer(int peer_device);
+/* n (1..8) copies dst[j][0:bytes[j]) = src[j][0:bytes[j]) in one kernel:
+ * SMs of the current GPU load src (its own memory) and store to dst, which
+ * may be another GPU's memory (peer stores over NVLink).  16-byte aligned
+ * pointers; ctas_per_job <= 0 picks 2 * SMs / n. */
+int cmb_p2p_scatter_store(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                          int ctas_per_job, cmb_stream_t stream);
+/* The same n copies by the copy engines (cudaMemcpyAsync, one internal
+ * stream per job, joined back into `stream`). */
+int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src, const size_t *bytes,
+                                int n, cmb_stream_t stream);
+
 /* --- checks ---------------------------------------------------------- */
 
 /* *mismatches (device) = 0 iff a[0:bytes) == b[0:bytes) (otherwise the

@@ -1,0 +1,102 @@
+"""GPU tests of the NVLink probe: the scatter kernels and copy-engine
+scatter are bit-exact (local destinations on one GPU); with two or more GPUs
+the CLI's --p2p section and a two-process IPC exchange deliver every byte."""
+
+import ctypes
+import json
+import os
+import socket
+import subprocess
+
+import pytest
+
+from tests.helpers import dptr, stream_handle
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+EXE = os.path.join(ROOT, "cuda_micro_bench_b200", "bin", "cmb_b200")
+
+
+@pytest.mark.parametrize("method", ["store", "copy_engine"])
+@pytest.mark.parametrize("sizes", [[1 << 20], [4096 + 48, 7 << 16, 16], [5 << 20] * 8])
+def test_scatter_local_bit_exact(cuda, cmb, method, sizes):
+    n = len(sizes)
+    src = [cuda.randint(0, 255, (s,), dtype=cuda.uint8, device="cuda") for s in sizes]
+    dst = [cuda.zeros(s + 64, dtype=cuda.uint8, device="cuda") for s in sizes]
+    d = (ctypes.c_void_p * n)(*[t.data_ptr() for t in dst])
+    s_ = (ctypes.c_void_p * n)(*[t.data_ptr() for t in src])
+    nb = (ctypes.c_size_t * n)(*sizes)
+    if method == "store":
+        cmb.check("cmb_p2p_scatter_store", d, s_, nb, n, 0, stream_handle(cuda))
+    else:
+        cmb.check("cmb_p2p_scatter_copy_engine", d, s_, nb, n, stream_handle(cuda))
+    cuda.cuda.synchronize()
+    for a, b, sz in zip(src, dst, sizes):
+        assert cuda.equal(a, b[:sz])
+        assert int(b[sz:].count_nonzero()) == 0
+
+
+def test_cli_p2p_section(cuda, tmp_path):
+    out = tmp_path / "r.json"
+    p = subprocess.run([EXE, "--p2p", f"--out={out}"], capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stdout + p.stderr
+    res = json.loads(out.read_text())["results"]
+    count = cuda.cuda.device_count()
+    assert res["pcie"]["device_count"]["value"] == count
+    if count >= 2:
+        for k in ("ring_store", "ring_copy_engine", "alltoall_store", "alltoall_copy_engine"):
+            assert res["p2p"][k + "_verified"]["value"] == 1.0
+            assert res["p2p"][k + "_link_gbps"]["value"] > 10.0
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank(rank, world, port, q):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
+                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank), "NCCL_NVLS_ENABLE": "0"})
+    import torch
+
+    torch.cuda.set_device(rank)
+    import bench
+    from cuda_micro_bench_b200 import multi_gpu
+
+    ranks = bench.Ranks("nccl")
+    ex = multi_gpu.PeerExchange(ranks, 16 << 20, 77)
+    bad = {}
+    sh = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for mode in ("ring", "alltoall"):
+        for method in ("store", "copy_engine"):
+            ranks.barrier()
+            ex.launch(mode, method, sh)
+            torch.cuda.synchronize()
+            ranks.barrier()
+            bad[(mode, method)] = ex.mismatches(mode, sh)
+    ex.close()
+    ranks.close()
+    q.put((rank, bad))
+
+
+def test_two_process_ipc_exchange(cuda):
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, bad in res:
+        assert all(v == 0 for v in bad.values()), (rank, bad)
