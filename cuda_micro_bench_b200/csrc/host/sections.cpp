@@ -724,6 +724,8 @@ int multi_gpu_body(std::vector<GpuSide> &g, size_t bytes) {
 }  // namespace
 
 int benchmark_multi_gpu() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
   int count = 0;
   CMB_CUDA_TRY(cudaGetDeviceCount(&count));
   printf("=== Multi-GPU (NVLink P2P) ===\n");
