@@ -446,8 +446,8 @@ def probe_tma(torch, stream, sh, peaks):
 
 def probe_gemm(torch, stream, sh, peaks):
     """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5, fp32 accumulation in
-    TMEM, 2-CTA 256x256 tiles (and the 1-CTA 128x256 form); FP8 e4m3 with a
-    per-tensor scale.  TFLOP/s = 2*M*N*K / median launch time; 8 sampled
+    TMEM, 2-CTA tiles of 256 x 512 (two N=256 accumulators per pair), and the
+    1-CTA 128x256 form; FP8 e4m3 with a per-tensor scale.  TFLOP/s = 2*M*N*K / median launch time; 8 sampled
     64x64 output tiles are checked against an fp64 product."""
     from cuda_micro_bench_b200 import check
 

@@ -20,11 +20,15 @@
 //               accumulators (2 x 256 columns) let the epilogue of tile j
 //               overlap the MMAs of tile j+1.
 // CG = 1: tile 128 x 256 per CTA (cta_group::1, MMA M=128 N=256).
-// CG = 2: a cluster of two CTAs computes a 256 x 256 tile with
+// CG = 2: a cluster of two CTAs computes a 256 x (256 * NSUB) tile with
 //   cta_group::2 MMAs (M=256 N=256) issued by CTA 0; each CTA loads its own
-//   128 rows of A and 128 rows of B (N), the loads of both CTAs complete on
-//   CTA 0's full barrier, and CTA 0 commits to both CTAs' barriers one
-//   address at a time.
+//   128 rows of A and 128 rows of each N=256 slice of B, the loads of both
+//   CTAs complete on CTA 0's full barrier, and CTA 0 commits to both CTAs'
+//   barriers one address at a time.  NSUB = 2 (the default) issues two MMAs
+//   per K slice into all 512 TMEM columns: a quarter fewer bytes loaded per
+//   FLOP than 256 x 256 tiles, at the cost of the epilogue no longer
+//   overlapping the next tile's MMAs (on B200 the load savings win: ~1.5
+//   PFLOP/s bf16 against ~1.2 for 256 x 256).
 // All waits are bounded; a wait that gives up reports CMB_ERR_TIMEOUT in
 // `status` and every role drains and leaves.
 #include <cuda.h>
@@ -42,25 +46,31 @@ int make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, 
 
 namespace {
 
-template <int CG, bool kFp8, int STAGES, bool kTmaEpi>
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW>
 struct GemmCfg {
-  static constexpr int kThreads = 192;
+  static constexpr int kEpiWarps = EPIW;             // epilogue warps: 4 or 8
+  static constexpr int kThreads = 64 + 32 * EPIW;
   static constexpr int kBmCta = 128;                 // A rows per CTA
-  static constexpr int kBn = 256;                    // MMA N = output columns per tile
-  static constexpr int kBnCta = kBn / CG;            // B rows loaded per CTA
+  static constexpr int kBn = 256;                    // MMA N
+  static constexpr int kTileN = kBn * NSUB;          // output columns per tile
+  static constexpr int kBnCta = kBn / CG;            // B rows per N=256 sub-tile per CTA
   static constexpr int kKBytes = 128;                // K bytes per stage (one swizzle row)
   static constexpr int kElem = kFp8 ? 1 : 2;
   static constexpr int kBk = kKBytes / kElem;        // K elements per stage
   static constexpr int kMmaPerStage = 4;             // 32 bytes of K per instruction
   static constexpr int kABytes = kBmCta * kKBytes;   // 16 KiB
-  static constexpr int kBBytes = kBnCta * kKBytes;   // 32 KiB (CG=1) / 16 KiB (CG=2)
+  static constexpr int kBSubBytes = kBnCta * kKBytes;  // 32 KiB (CG=1) / 16 KiB (CG=2)
+  static constexpr int kBBytes = NSUB * kBSubBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = STAGES;
   static constexpr int kTileM = kBmCta * CG;         // output rows per tile
-  static constexpr int kTmemCols = 512;              // two 256-column accumulators
+  static constexpr int kTmemCols = 512;              // all of TMEM
+  // 256-column tiles keep two accumulators (the epilogue of one tile
+  // overlaps the MMAs of the next); 512-column tiles use all 512 columns.
+  static constexpr int kAccBufs = 2 / NSUB;
   // TMA-store epilogue: per epilogue warp two 32 x 32 fp32 staging boxes.
   static constexpr int kEpiBoxBytes = 32 * 32 * 4;
-  static constexpr int kEpiBytes = kTmaEpi ? 4 * 2 * kEpiBoxBytes : 0;
+  static constexpr int kEpiBytes = kTmaEpi ? EPIW * 2 * kEpiBoxBytes : 0;
   static constexpr size_t kSmem = (size_t)kStages * kStageBytes + kEpiBytes + 1024;
   static constexpr uint32_t kIdesc = tc::instr_desc<kTileM, kBn, kFp8>();
 };
@@ -84,12 +94,12 @@ __device__ __forceinline__ void st_cs_f4(float *p, float a, float b, float c, fl
                : "memory");
 }
 
-template <int CG, bool kFp8, int STAGES, bool kTmaEpi>
-__global__ void __launch_bounds__(192, 1)
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW>
+__global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
            const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M, int N, int K,
            const float *scale_a, const float *scale_b, int group_m, int *status) {
-  using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi>;
+  using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
@@ -108,7 +118,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       dev::mbar_init(dev::smem_addr(&tfull[a]), 1);
-      dev::mbar_init(dev::smem_addr(&tempty[a]), 4 * CG);
+      dev::mbar_init(dev::smem_addr(&tempty[a]), EPIW * CG);
     }
     dev::mbar_init(dev::smem_addr(&mma_done), 1);
     abort_flag = 0;
@@ -128,7 +138,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = tmem_holder;
 
   const int tiles_m = (M + Cfg::kTileM - 1) / Cfg::kTileM;
-  const int tiles_n = (N + Cfg::kBn - 1) / Cfg::kBn;
+  const int tiles_n = (N + Cfg::kTileN - 1) / Cfg::kTileN;
   const int tiles = tiles_m * tiles_n;
   const int cluster = blockIdx.x / CG, nclusters = gridDim.x / CG;
   const int kblocks = (K + Cfg::kBk - 1) / Cfg::kBk;
@@ -142,7 +152,7 @@ __global__ void __launch_bounds__(192, 1)
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
         const int a_row = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta;
-        const int b_row = tn * Cfg::kBn + static_cast<int>(rank) * Cfg::kBnCta;
+        const int b_row = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBnCta;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % Cfg::kStages;
           const uint32_t ph = (it / Cfg::kStages) & 1;
@@ -157,15 +167,23 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t *b_dst = a_dst + Cfg::kABytes;
           const int kx = kb * Cfg::kBk;
           const uint32_t bar = dev::smem_addr(&full[s]);
+          // B sub-tile u covers output columns [u * 256, u * 256 + 256) of the
+          // tile; this CTA loads its kBnCta rows of each.
           if constexpr (CG == 1) {
             dev::mbar_arrive_expect_tx(bar, Cfg::kStageBytes);
             dev::tma_load_2d(dev::smem_addr(a_dst), &tmA, kx, a_row, bar);
-            dev::tma_load_2d(dev::smem_addr(b_dst), &tmB, kx, b_row, bar);
+#pragma unroll
+            for (int u = 0; u < NSUB; ++u)
+              dev::tma_load_2d(dev::smem_addr(b_dst + u * Cfg::kBSubBytes), &tmB, kx,
+                               b_row + u * Cfg::kBn, bar);
           } else {
             const uint32_t leader_bar = tc::map_to_cta(bar, 0);
             if (rank == 0) dev::mbar_arrive_expect_tx(bar, 2 * Cfg::kStageBytes);
             tc::tma_load_2d_pair(dev::smem_addr(a_dst), &tmA, kx, a_row, leader_bar);
-            tc::tma_load_2d_pair(dev::smem_addr(b_dst), &tmB, kx, b_row, leader_bar);
+#pragma unroll
+            for (int u = 0; u < NSUB; ++u)
+              tc::tma_load_2d_pair(dev::smem_addr(b_dst + u * Cfg::kBSubBytes), &tmB, kx,
+                                   b_row + u * Cfg::kBn, leader_bar);
           }
         }
       }
@@ -176,15 +194,15 @@ __global__ void __launch_bounds__(192, 1)
       int it = 0, j = 0;
       bool ok = true;
       for (int t = cluster; t < tiles && ok; t += nclusters, ++j) {
-        const int a = j & 1;
-        const uint32_t aph = (j >> 1) & 1;
+        const int a = j % Cfg::kAccBufs;
+        const uint32_t aph = (j / Cfg::kAccBufs) & 1;
         if (!dev::mbar_wait_bounded(dev::smem_addr(&tempty[a]), aph ^ 1)) {
           dev::report_status(status, CMB_ERR_TIMEOUT);
           atomicExch(&abort_flag, 1);
           break;
         }
         tc::fence_after_sync();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(a * Cfg::kBn);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(a * Cfg::kTileN);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % Cfg::kStages;
           const uint32_t ph = (it / Cfg::kStages) & 1;
@@ -201,7 +219,11 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t db = tc::sw128_kmajor_desc(a_addr + Cfg::kABytes);
 #pragma unroll
           for (int k = 0; k < Cfg::kMmaPerStage; ++k)
-            tc::mma<CG, kFp8>(d, da + 2 * k, db + 2 * k, Cfg::kIdesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int u = 0; u < NSUB; ++u)
+              tc::mma<CG, kFp8>(d + u * Cfg::kBn, da + 2 * k,
+                                db + (u * Cfg::kBSubBytes >> 4) + 2 * k, Cfg::kIdesc,
+                                (kb | k) != 0 ? 1u : 0u);
           const uint32_t eb = dev::smem_addr(&empty[s]);
           tc::commit<CG>(eb);
           if constexpr (CG == 2) tc::commit<CG>(tc::map_to_cta(eb, 1));
@@ -218,18 +240,23 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    // Warp w reads TMEM lane quarter w % 4; with 8 epilogue warps two warps
+    // share a quarter and split its columns in halves.
+    const int q = warp & 3;
+    const int ew = warp - 2;
+    constexpr int kChunks = Cfg::kTileN / 32 / (EPIW / 4);  // 32-column chunks per warp
+    const int c_begin = (ew / 4) * kChunks;
     float scale = 1.0f;
     if constexpr (kFp8) scale = __ldg(scale_a) * __ldg(scale_b);
     const bool vec_ok = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
-    uint8_t *epi = ring + (size_t)Cfg::kStages * Cfg::kStageBytes + (size_t)q * 2 * Cfg::kEpiBoxBytes;
+    uint8_t *epi = ring + (size_t)Cfg::kStages * Cfg::kStageBytes + (size_t)ew * 2 * Cfg::kEpiBoxBytes;
     uint32_t epi_count = 0;
     int j = 0;
     for (int t = cluster; t < tiles; t += nclusters, ++j) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
-      const int a = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
+      const int a = j % Cfg::kAccBufs;
+      const uint32_t ph = (j / Cfg::kAccBufs) & 1;
       if (!dev::mbar_wait_bounded(dev::smem_addr(&tfull[a]), ph) ||
           *(volatile int *)&abort_flag) {
         dev::report_status(status, CMB_ERR_TIMEOUT);
@@ -240,14 +267,14 @@ __global__ void __launch_bounds__(192, 1)
       const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta + q * 32;
       const int row = row0 + lane;
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * Cfg::kBn);
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * Cfg::kTileN);
       float *crow = C + (size_t)row * N;
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kBn / 32; ++c) {
+      for (int c = c_begin; c < c_begin + kChunks; ++c) {
         uint32_t r[32];
         tc::ld_32x32b_x32(taddr + c * 32, r);
         tc::wait_ld();
-        if (c == Cfg::kBn / 32 - 1) {
+        if (c == c_begin + kChunks - 1) {
           // every TMEM read of this accumulator is done: hand it back
           tc::fence_before_sync();
           __syncwarp();
@@ -257,7 +284,7 @@ __global__ void __launch_bounds__(192, 1)
             else dev::mbar_arrive_cluster(tc::map_to_cta(eb, 0));
           }
         }
-        const int col0 = tn * Cfg::kBn + c * 32;
+        const int col0 = tn * Cfg::kTileN + c * 32;
         if constexpr (kTmaEpi) {
           // Stage the warp's 32 x 32 box in shared memory (128-byte
           // swizzle: 16-byte chunk j of row r at (j ^ (r % 8)) * 16, which
@@ -346,11 +373,11 @@ __global__ void k_quantize_e4m3(const __nv_bfloat16 *__restrict__ x, size_t n,
     scale_out[0] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
 }
 
-template <int CG, bool kFp8, int STAGES, bool kTmaEpi>
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW>
 int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
                 const float *scale_a, const float *scale_b, int group_m, int *status,
                 cudaStream_t stream) {
-  using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi>;
+  using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
   const CUtensorMapDataType dt =
       kFp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta, tb;
@@ -368,10 +395,10 @@ int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
   } else {
     tcm = ta;  // unused
   }
-  auto kern = k_gemm<CG, kFp8, STAGES, kTmaEpi>;
+  auto kern = k_gemm<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
   CMB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(Cfg::kSmem)));
-  const int tiles = ((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kBn - 1) / Cfg::kBn);
+  const int tiles = ((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   int clusters = current_sm_count() / CG;
   if (clusters > tiles) clusters = tiles;
   if (group_m <= 0) group_m = 8;
@@ -409,35 +436,44 @@ int gemm_checks(const char *fn, const void *A, const void *B, const float *C, in
 }
 
 // Default shapes (from sweeps on B200 against cuBLAS measured alongside):
-// 1-CTA 128x256 tiles with 4 stages of 48 KiB; 2-CTA 256x256 tiles with 4
-// stages of 32 KiB per CTA; raster groups of 8 tile rows; the TMA-store
-// epilogue whenever C's row pitch allows a tensor map (N % 4 == 0, 16-byte
-// aligned C).
+// 1-CTA 128x256 tiles with 4 stages of 48 KiB; 2-CTA 256x512 tiles with 4
+// stages of 48 KiB per CTA; raster groups of 8 tile rows; 4 epilogue warps;
+// the TMA-store epilogue whenever C's row pitch allows a tensor map
+// (N % 4 == 0, 16-byte aligned C).
 template <bool kFp8, bool kTmaEpi>
 int dispatch_stages(const void *A, const void *B, float *C, int M, int N, int K,
                     const float *scale_a, const float *scale_b, int cta_group, int stages,
-                    int group_m, int *status, cudaStream_t stream) {
-#define CMB_GEMM_CASE(CGV, S)                                                                \
-  if (cta_group == CGV && stages == S)                                                      \
-    return launch_gemm<CGV, kFp8, S, kTmaEpi>(A, B, C, M, N, K, scale_a, scale_b, group_m,  \
-                                              status, stream);
+                    int group_m, int tile_n, int epi_warps, int *status, cudaStream_t stream) {
+#define CMB_GEMM_CASE(CGV, S, NS, EW)                                                          \
+  if (cta_group == CGV && stages == S && tile_n == 256 * NS && epi_warps == EW)               \
+    return launch_gemm<CGV, kFp8, S, kTmaEpi, NS, EW>(A, B, C, M, N, K, scale_a, scale_b,      \
+                                                      group_m, status, stream);
+  if (tile_n == 0) tile_n = cta_group == 2 ? 512 : 256;
   if (stages == 0) stages = 4;
-  CMB_GEMM_CASE(1, 3)
-  CMB_GEMM_CASE(1, 4)
-  CMB_GEMM_CASE(2, 4)
-  CMB_GEMM_CASE(2, 5)
-  CMB_GEMM_CASE(2, 6)
-  if constexpr (!kTmaEpi) { CMB_GEMM_CASE(2, 7) }
+  if (epi_warps == 0) epi_warps = 4;
+  CMB_GEMM_CASE(1, 3, 1, 4)
+  CMB_GEMM_CASE(1, 4, 1, 4)
+  CMB_GEMM_CASE(2, 4, 1, 4)
+  CMB_GEMM_CASE(2, 5, 1, 4)
+  CMB_GEMM_CASE(2, 6, 1, 4)
+  CMB_GEMM_CASE(2, 3, 2, 4)
+  CMB_GEMM_CASE(2, 4, 2, 4)
+  CMB_GEMM_CASE(2, 3, 2, 8)
+  if constexpr (!kTmaEpi) {
+    CMB_GEMM_CASE(2, 7, 1, 4)
+    CMB_GEMM_CASE(2, 4, 2, 8)
+  }
 #undef CMB_GEMM_CASE
   return fail(CMB_ERR_INVALID_ARG,
-              "gemm: stages %d not available for cta_group %d (1: 3-4; 2: 4-6, or 7 with the "
-              "direct-store epilogue)", stages, cta_group);
+              "gemm: no kernel for cta_group %d, %d stages, tile_n %d, %d epilogue warps",
+              cta_group, stages, tile_n, epi_warps);
 }
 
 template <bool kFp8>
 int dispatch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
                   const float *scale_a, const float *scale_b, int cta_group, int stages,
-                  int group_m, int epilogue, int *status, cudaStream_t stream) {
+                  int group_m, int epilogue, int tile_n, int epi_warps, int *status,
+                  cudaStream_t stream) {
   const bool tma_ok = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
   if (epilogue == 0) epilogue = tma_ok ? 2 : 1;
   if (epilogue == 2 && !tma_ok)
@@ -445,10 +481,10 @@ int dispatch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
                 "16-byte aligned C");
   if (epilogue == 2)
     return dispatch_stages<kFp8, true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, stages,
-                                       group_m, status, stream);
+                                       group_m, tile_n, epi_warps, status, stream);
   if (epilogue == 1)
     return dispatch_stages<kFp8, false>(A, B, C, M, N, K, scale_a, scale_b, cta_group, stages,
-                                        group_m, status, stream);
+                                        group_m, tile_n, epi_warps, status, stream);
   return fail(CMB_ERR_INVALID_ARG, "gemm: epilogue %d not in {0, 1, 2}", epilogue);
 }
 
@@ -462,14 +498,14 @@ extern "C" int cmb_gemm_bf16(const void *A, const void *B, float *C, int M, int 
   int rc = gemm_checks("cmb_gemm_bf16", A, B, C, M, N, K, 2, cta_group);
   if (rc) return rc;
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
-  return dispatch_gemm<false>(A, B, C, M, N, K, nullptr, nullptr, cta_group, 0, 0, 0, status,
-                              stream);
+  return dispatch_gemm<false>(A, B, C, M, N, K, nullptr, nullptr, cta_group, 0, 0, 0, 0, 0,
+                              status, stream);
 }
 
 extern "C" int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int N, int K,
                               int fp8, const float *scale_a, const float *scale_b, int cta_group,
-                              int stages, int group_m, int epilogue, int *status,
-                              cmb_stream_t stream) {
+                              int stages, int group_m, int epilogue, int tile_n, int epi_warps,
+                              int *status, cmb_stream_t stream) {
   int rc = gemm_checks("cmb_gemm_tuned", A, B, C, M, N, K, fp8 ? 1 : 2, cta_group);
   if (rc) return rc;
   if (fp8 && (scale_a == nullptr || scale_b == nullptr))
@@ -477,9 +513,9 @@ extern "C" int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int
   if (group_m < 0) return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_tuned: group_m < 0");
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
   return fp8 ? dispatch_gemm<true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, stages, group_m,
-                                   epilogue, status, stream)
+                                   epilogue, tile_n, epi_warps, status, stream)
              : dispatch_gemm<false>(A, B, C, M, N, K, nullptr, nullptr, cta_group, stages,
-                                    group_m, epilogue, status, stream);
+                                    group_m, epilogue, tile_n, epi_warps, status, stream);
 }
 
 extern "C" int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
@@ -490,8 +526,8 @@ extern "C" int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int 
   if (scale_a == nullptr || scale_b == nullptr)
     return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_e4m3: null scale");
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
-  return dispatch_gemm<true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, 0, 0, 0, status,
-                             stream);
+  return dispatch_gemm<true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, 0, 0, 0, 0, 0,
+                             status, stream);
 }
 
 extern "C" int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst,

@@ -175,8 +175,8 @@ int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint32_t *out_c
 /* C[M x N] (fp32, row-major) = A[M x K] * B[N x K]^T for bf16 A, B stored
  * K-major (row-major with K contiguous; the "row.col" operand order of
  * src/tensor_core_extended.cu:116), fp32 accumulation in tensor memory.
- * cta_group 1: 128 x 256 tiles per CTA; 2: 256 x 256 tiles per pair of CTAs
- * (cta_group::2 MMAs).  Needs K % 8 == 0 and 16-byte aligned A, B.
+ * cta_group 1: 128 x 256 tiles per CTA; 2: 256 x 512 tiles per pair of CTAs
+ * (cta_group::2 MMAs, two N = 256 accumulators filling TMEM).  Needs K % 8 == 0 and 16-byte aligned A, B.
  * Replaces the register-only mma.sync throughput kernels
  * (src/tensor_core_extended.cu:77-128,265-292) with a GEMM that reads and
  * writes memory and has a checkable result. */
@@ -192,10 +192,15 @@ int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
  * pipeline shape, for sweeps: stages 3-4 (cta_group 1) or 4-6 (cta_group 2;
  * 7 with epilogue 1), 0 = default (4); group_m = tile rows per raster
  * group, 0 = default (8); epilogue 1 = direct stores, 2 = TMA stores (needs
- * N % 4 == 0), 0 = default (2 when possible). */
+ * N % 4 == 0), 0 = default (2 when possible); tile_n = output columns per
+ * tile, 256 or (cta_group 2, stages 3-4) 512 = two N=256 MMAs per K slice
+ * into all 512 TMEM columns, 0 = default (512 for cta_group 2, else 256);
+ * epi_warps = epilogue warps, 4 or (tile_n 512, stages 3, or stages 4 with
+ * epilogue 1) 8, 0 = default (4). */
 int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int N, int K, int fp8,
                    const float *scale_a, const float *scale_b, int cta_group, int stages,
-                   int group_m, int epilogue, int *status, cmb_stream_t stream);
+                   int group_m, int epilogue, int tile_n, int epi_warps, int *status,
+                   cmb_stream_t stream);
 /* Tensor-pipe ceiling: `ctas` CTAs (one per SM) each issue `iters` rounds of
  * four tcgen05.mma M=128 N=256 (bf16: fp8 = 0, K = 16; e4m3: fp8 = 1,
  * K = 32) on all-ones operands resident in shared memory, into TMEM, with no

@@ -126,9 +126,11 @@ def test_gemm_e4m3(cuda, cmb, orc, cg, M, N, K):
 
 
 @pytest.mark.parametrize("fp8", [0, 1])
-@pytest.mark.parametrize("cg,stages,epi", [(1, 3, 1), (1, 4, 2), (2, 4, 1), (2, 5, 2), (2, 6, 2),
-                                           (2, 7, 1)])
-def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi):
+@pytest.mark.parametrize("cg,stages,epi,tile_n,ew", [
+    (1, 3, 1, 256, 4), (1, 4, 2, 256, 4), (2, 4, 1, 256, 4), (2, 5, 2, 256, 4), (2, 6, 2, 256, 4),
+    (2, 7, 1, 256, 4), (2, 3, 2, 512, 4), (2, 4, 2, 512, 4), (2, 4, 1, 512, 4), (2, 3, 2, 512, 8),
+    (2, 4, 1, 512, 8)])
+def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi, tile_n, ew):
     M, N, K = 700, 520, 1040
     A = _normal_bf16(cuda, cmb, M, K, 31, K ** -0.5)
     B = _normal_bf16(cuda, cmb, N, K, 32, K ** -0.5)
@@ -138,12 +140,12 @@ def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi):
         qa, sa = _quantize(cuda, cmb, A)
         qb, sb = _quantize(cuda, cmb, B)
         cmb.check("cmb_gemm_tuned", dptr(qa), dptr(qb), dptr(C), M, N, K, 1, dptr(sa), dptr(sb), cg,
-                  stages, 4, epi, dptr(status), stream_handle(cuda))
+                  stages, 4, epi, tile_n, ew, dptr(status), stream_handle(cuda))
         a_h, b_h, dt = qa.cpu().numpy(), qb.cpu().numpy(), 1
         s_a, s_b = float(sa[0].item()), float(sb[0].item())
     else:
         cmb.check("cmb_gemm_tuned", dptr(A), dptr(B), dptr(C), M, N, K, 0, None, None, cg, stages,
-                  4, epi, dptr(status), stream_handle(cuda))
+                  4, epi, tile_n, ew, dptr(status), stream_handle(cuda))
         a_h, b_h, dt = A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16), 0
         s_a = s_b = 1.0
     cuda.cuda.synchronize()
@@ -165,7 +167,7 @@ def test_gemm_ragged_columns(cuda, cmb, orc, cg, epi, M, N, K):
     status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
     for _ in range(3):
         cmb.check("cmb_gemm_tuned", dptr(A), dptr(B), dptr(C), M, N, K, 0, None, None, cg, 0, 0, epi,
-                  dptr(status), stream_handle(cuda))
+                  0, 0, dptr(status), stream_handle(cuda))
         cuda.cuda.synchronize()
         assert int(status.item()) == 0
         _check_tiles(orc, A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16),
@@ -198,6 +200,8 @@ def test_gemm_rejects_bad_args(cuda, cmb):
                                  s) == 1
     # TMA-store epilogue needs N % 4 == 0; 7 stages only with direct stores
     assert cmb.lib.cmb_gemm_tuned(dptr(a), dptr(a), dptr(c), 16, 18, 16, 0, None, None, 2, 4, 0, 2,
-                                  None, s) == 1
+                                  0, 0, None, s) == 1
     assert cmb.lib.cmb_gemm_tuned(dptr(a), dptr(a), dptr(c), 16, 16, 16, 0, None, None, 2, 7, 0, 2,
-                                  None, s) == 1
+                                  0, 0, None, s) == 1
+    assert cmb.lib.cmb_gemm_tuned(dptr(a), dptr(a), dptr(c), 16, 16, 16, 0, None, None, 1, 4, 0, 2,
+                                  512, 0, None, s) == 1
