@@ -355,6 +355,81 @@ int benchmark_cache() {
   return CMB_OK;
 }
 
+// --memory-more: L2 aggregate read bandwidth (src/memory_more.cu:201-234):
+// an L2-resident buffer of min(8 MiB, L2/4) read 1024 times by 4 CTAs per
+// SM; median of five after one warm-up; the exact word sum is checked.
+int benchmark_memory_more() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== Memory (L2 aggregate bandwidth) ===\n");
+  const size_t bytes = std::min<size_t>(8ull << 20, (size_t)info.l2_cache_size / 4);
+  const int passes = 1024;
+  DevBuf buf, sum;
+  TRY(buf.alloc(bytes));
+  TRY(sum.alloc(sizeof(unsigned long long)));
+  TRY(cmb_fill_hash_u32(buf.as<uint32_t>(), bytes / 4, nullptr));
+  double ms = 0;
+  TRY(time_median([&] { return cmb_l2_read(buf.p, bytes, passes, 0, sum.as<unsigned long long>(), nullptr); },
+                  6, 1, &ms));
+  unsigned long long got = 0, words = 0;
+  CMB_CUDA_TRY(cudaMemcpy(&got, sum.p, sizeof(got), cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < bytes / 4; ++i) {
+    uint32_t x = static_cast<uint32_t>(i) + 0x9e3779b9u;
+    x = (x ^ (x >> 16)) * 0x85ebca6bu;
+    x = (x ^ (x >> 13)) * 0xc2b2ae35u;
+    words += x ^ (x >> 16);
+  }
+  if (got != words * passes)
+    return fail(CMB_ERR_MISMATCH, "L2 read: word sum %llu != %llu", got, words * passes);
+  const double total = (double)bytes * passes;
+  printf("  L2 aggregate BW (%zu KiB resident, .cg 16-byte loads): %.2f GiB/s (%.1f GB/s)\n",
+         bytes >> 10, gib_per_s(total, ms), gb_per_s(total, ms));
+  g_results.log("memory_more", "l2_aggregate_bw_gibps", gib_per_s(total, ms), "GiB/s");
+  g_results.log("memory_more", "l2_aggregate_bw_gbps", gb_per_s(total, ms), "GB/s");
+  g_results.log("memory_more", "l2_aggregate_working_set_bytes", (double)bytes, "bytes");
+  g_results.log("memory_more", "l2_aggregate_verified", 1.0, "bool");
+  return CMB_OK;
+}
+
+// --pcie: pinned host <-> device copy bandwidth (src/pcie.cu:55-97): 64 MiB,
+// ten copies per direction after a warm-up, device-timed.
+int benchmark_pcie() {
+  DeviceInfo info;
+  TRY(query_device(0, &info));
+  printf("=== PCIe (pinned host <-> device) ===\n");
+  const size_t bytes = 64ull << 20;
+  void *host = nullptr;
+  CMB_CUDA_TRY(cudaMallocHost(&host, bytes));
+  DevBuf dev;
+  int rc = dev.alloc(bytes);
+  double h2d = 0, d2h = 0;
+  if (rc == CMB_OK) {
+    std::memset(host, 0x5a, bytes);
+    rc = time_median(
+        [&]() -> int {
+          for (int r = 0; r < 10; ++r)
+            CMB_CUDA_TRY(cudaMemcpyAsync(dev.p, host, bytes, cudaMemcpyHostToDevice, nullptr));
+          return CMB_OK;
+        },
+        2, 1, &h2d);
+  }
+  if (rc == CMB_OK)
+    rc = time_median(
+        [&]() -> int {
+          for (int r = 0; r < 10; ++r)
+            CMB_CUDA_TRY(cudaMemcpyAsync(host, dev.p, bytes, cudaMemcpyDeviceToHost, nullptr));
+          return CMB_OK;
+        },
+        2, 1, &d2h);
+  cudaFreeHost(host);
+  if (rc != CMB_OK) return rc;
+  const double up = gib_per_s(10.0 * bytes, h2d), down = gib_per_s(10.0 * bytes, d2h);
+  printf("  HtoD pinned bandwidth: %.2f GiB/s\n  DtoH pinned bandwidth: %.2f GiB/s\n", up, down);
+  g_results.log("pcie", "htod_bandwidth_GiB_s", up, "GiB/s");
+  g_results.log("pcie", "dtoh_bandwidth_GiB_s", down, "GiB/s");
+  return CMB_OK;
+}
+
 int benchmark_tma() {
   DeviceInfo info;
   TRY(query_device(0, &info));
@@ -556,7 +631,7 @@ int benchmark_tensor_core_extended() {
     const double tf = flop / (ms * 1e-3) / 1e12;
     const double spec = fp8 ? 4500.0 : 2250.0;
     const std::string p = fp8 ? "fp8_e4m3_gemm_8192" : "bf16_gemm_8192";
-    printf("  tcgen05 %s GEMM 8192^3 (2-CTA 256x256): %.1f TFLOP/s (%.1f%% of %.0f), sampled "
+    printf("  tcgen05 %s GEMM 8192^3 (2-CTA 256x512): %.1f TFLOP/s (%.1f%% of %.0f), sampled "
            "rel err %.1e\n", fp8 ? "e4m3" : "bf16", tf, 100 * tf / spec, spec, err);
     if (err > 1e-2) return fail(CMB_ERR_MISMATCH, "%s: sampled rel err %.3g > 1e-2", p.c_str(), err);
     g_results.log("tensor_core_tcgen05", p + "_tflops", tf, "TFLOP/s");
@@ -766,6 +841,8 @@ const Section kSections[] = {
     {"--device", "Device / SM info and derived peaks", benchmark_device_info},
     {"--memory", "HBM read/copy streams and DRAM pointer chase", benchmark_global_memory},
     {"--cache", "L1/L2 dependent-load latency sweep", benchmark_cache},
+    {"--memory-more", "L2 aggregate read bandwidth", benchmark_memory_more},
+    {"--pcie", "Pinned host <-> device copy bandwidth", benchmark_pcie},
     {"--tma", "TMA bulk-tensor latency, tile load and tile copy", benchmark_tma},
     {"--tensor", "mma.sync TF32 and tcgen05 issue-rate probes", benchmark_tensor_core},
     {"--tensor-ext", "mma.sync FP16/BF16/FP8/INT8 and tcgen05 BF16/FP8 GEMM", benchmark_tensor_core_extended},

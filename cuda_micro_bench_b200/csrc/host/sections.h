@@ -34,6 +34,8 @@ int query_device(int dev, DeviceInfo *info);
 
 int benchmark_global_memory();       // --memory      (src/mem_global.cu:27-75)
 int benchmark_cache();               // --cache       (src/mem_cache.cu:4-24)
+int benchmark_memory_more();         // --memory-more (src/memory_more.cu:201-234, L2 only)
+int benchmark_pcie();                // --pcie        (src/pcie.cu:55-97, bandwidth only)
 int benchmark_tma();                 // --tma         (src/tma.cu:157-259)
 int benchmark_tensor_core();         // --tensor      (src/tensor_core.cu:66-120)
 int benchmark_tensor_core_extended();  // --tensor-ext (src/tensor_core_extended.cu:321-357)

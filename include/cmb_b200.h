@@ -108,6 +108,14 @@ int cmb_stream_sum_f32_noalloc(const float *src, size_t n, double *out_sum, cmb_
 /* Capacity of that array in per-CTA partials (4096). */
 size_t cmb_stream_sum_noalloc_max_ctas(void);
 
+/* L2 aggregate read bandwidth: ctas CTAs (<= 0: 4 per SM) of 256 threads
+ * read buf[0:bytes) `passes` times with 16-byte ld.global.cg (L1 bypassed;
+ * size the buffer to stay in L2); *sum (device) = passes * (sum of the
+ * buffer's 32-bit words) mod 2^64.  Replaces kernel_l2_aggregate_bw
+ * (src/memory_more.cu:66-85), whose float sum is replaced by an exact one. */
+int cmb_l2_read(const void *buf, size_t bytes, int passes, int ctas, unsigned long long *sum,
+                cmb_stream_t stream);
+
 /* Host-buffer stream copy: host_dst = host_src through the device.  Copies
  * chunks host->device, runs cmb_stream_copy on each, copies them back, with
  * the three steps of consecutive chunks overlapped on three streams.

@@ -56,6 +56,9 @@ def test_cli_full_run(cuda, tmp_path):
     assert v("tensor_core_tcgen05", "fp8_e4m3_gemm_8192_tflops") > 1000
     assert v("tensor_core_extended", "fp16_m16n8k16_latency_cycles") > 0
     assert v("tensor_core", "mma_m16n8k8_throughput_tflops") > 0
+    assert v("memory_more", "l2_aggregate_verified") == 1.0
+    assert v("memory_more", "l2_aggregate_bw_gbps") > v("memory", "dram_read_bw_gbps")
+    assert 5 < v("pcie", "htod_bandwidth_GiB_s") < 128 and 5 < v("pcie", "dtoh_bandwidth_GiB_s") < 128
     print(p.stdout)
 
 

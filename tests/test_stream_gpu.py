@@ -140,3 +140,16 @@ def test_copy_host_buffers(cuda, cmb):
     b = cuda.empty(3 * chunk, dtype=cuda.uint8, device="cuda")
     cmb.check("cmb_stream_copy_host", hptr(dst), hptr(src), n, dptr(a), dptr(b), 3 * chunk, chunk)
     assert np.array_equal(src, dst)
+
+
+@pytest.mark.parametrize("nbytes,passes,ctas", [(16, 1, 1), (8 << 20, 4, 0), ((1 << 20) + 48, 3, 7)])
+def test_l2_read_exact_sum(cuda, cmb, orc, nbytes, passes, ctas):
+    words = nbytes // 4
+    d = cuda.empty(words, dtype=cuda.int32, device="cuda")
+    cmb.check("cmb_fill_hash_u32", dptr(d), words, stream_handle(cuda))
+    out = cuda.zeros(1, dtype=cuda.int64, device="cuda")
+    cmb.check("cmb_l2_read", dptr(d), nbytes, passes, ctas, dptr(out), stream_handle(cuda))
+    ref = np.empty(words, np.uint32)
+    orc.orc_fill_hash_u32(ptr(ref), words)
+    expect = (int(ref.astype(np.uint64).sum()) * passes) % (1 << 64)
+    assert int(out.cpu().numpy().view(np.uint64)[0]) == expect
