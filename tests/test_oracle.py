@@ -166,3 +166,39 @@ def test_quantize_e4m3(orc):
     # relative error of e4m3 normals is at most 2^-4
     big = np.abs(xf * inv) > 2.0**-6
     assert np.all(np.abs(back[big] - xf[big] * inv) <= np.abs(xf[big] * inv) * 2.0**-4)
+
+
+def _ref_fixtures():
+    import json
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ref_gpu_fixtures.json")
+    return json.load(open(path))
+
+
+def test_hash_fill_pinned_to_reference_kernel(orc):
+    """kernel_init_stream (src/mem_global.cu:5-12) run on a B200."""
+    ref = np.array(_ref_fixtures()["init_stream_4099"], dtype=np.uint32)
+    out = np.empty(ref.size, np.uint32)
+    orc.orc_fill_hash_u32(ptr(out), out.size)
+    assert np.array_equal(out, ref)
+
+
+def test_chase_walk_pinned_to_reference_kernel(orc):
+    """kernel_random_chase_cg (src/memory_chase.cu:29-34) on the oracle's
+    4096-slot Sattolo array (seed 0xC0DA): the endpoint after warmup + iters
+    hops equals the oracle's walk."""
+    links = np.empty(4096 * 32, np.uint32)
+    orc.orc_chase_build(ptr(links), links.nbytes, 0xC0DA)
+    for case in _ref_fixtures()["chase_cg"]:
+        assert orc.orc_chase_walk(ptr(links), case["warmup"] + case["iters"], 0) == case["final"]
+
+
+def test_constant_mma_sums_pinned_to_reference_kernels():
+    """The reference's all-ones mma.sync throughput kernels leave K * iters in
+    each accumulator (four per thread, summed); the legacy probes here check
+    the same per-accumulator value."""
+    fx = _ref_fixtures()
+    assert fx["stream_copy_1mib_identical"] is True
+    assert fx["hmma_bf16_sum_iters1000"] == 4 * 16 * 1000
+    assert fx["hmma_int8_sum_iters1000"] == 4 * 32 * 1000
