@@ -13,6 +13,7 @@
 // and no kernel waits on another GPU: completion is observed on the host.
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "cmb_device.cuh"
 #include "cmb_host.h"
@@ -29,37 +30,70 @@ struct Jobs {
   size_t bytes[kMaxJobs];
 };
 
+// 32-byte vector of the store kernel.
+struct V32 {
+  uint32_t w[8];
+};
+
+__device__ __forceinline__ V32 ld_v32(const void *p) {
+  V32 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]),
+                 "=r"(v.w[5]), "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_v32(void *p, const V32 &v) {
+  asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]),
+               "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]),
+               "r"(v.w[7])
+               : "memory");
+}
+
 // blockIdx.y = job; the CTAs of a job stride over its tiles of 256 threads
-// x 4 16-byte vectors: each thread keeps four loads of its own HBM in
-// flight, and each warp store instruction writes 512 contiguous bytes of the
-// destination.
+// x 4 vectors of VB bytes (16 or 32): each thread keeps four loads of its own
+// HBM in flight, and each warp store instruction writes 32 * VB contiguous
+// bytes of the destination.
+template <int VB>
 __global__ void __launch_bounds__(kP2PThreads) k_p2p_store(Jobs jobs) {
   constexpr int kUnroll = 4;
+  using V = typename std::conditional<VB == 16, uint4, V32>::type;
   const int j = blockIdx.y;
-  const uint4 *__restrict__ src = reinterpret_cast<const uint4 *>(jobs.src[j]);
-  uint4 *__restrict__ dst = reinterpret_cast<uint4 *>(jobs.dst[j]);
+  const char *__restrict__ src = jobs.src[j];
+  char *__restrict__ dst = jobs.dst[j];
   const size_t bytes = jobs.bytes[j];
-  const size_t nvec = bytes / 16;
+  const size_t nvec = bytes / VB;
   const size_t tile = (size_t)kP2PThreads * kUnroll;
   for (size_t base = blockIdx.x * tile; base < nvec; base += (size_t)gridDim.x * tile) {
     if (base + tile <= nvec) {
-      uint4 v[kUnroll];
+      V v[kUnroll];
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) v[k] = __ldg(src + base + k * kP2PThreads + threadIdx.x);
+      for (int k = 0; k < kUnroll; ++k) {
+        const size_t i = base + k * kP2PThreads + threadIdx.x;
+        if constexpr (VB == 16) v[k] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+        else v[k] = ld_v32(src + i * 32);
+      }
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) dst[base + k * kP2PThreads + threadIdx.x] = v[k];
+      for (int k = 0; k < kUnroll; ++k) {
+        const size_t i = base + k * kP2PThreads + threadIdx.x;
+        if constexpr (VB == 16) reinterpret_cast<uint4 *>(dst)[i] = v[k];
+        else st_v32(dst + i * 32, v[k]);
+      }
     } else {
       for (int k = 0; k < kUnroll; ++k) {
         const size_t i = base + k * kP2PThreads + threadIdx.x;
-        if (i < nvec) dst[i] = __ldg(src + i);
+        if (i < nvec) {
+          if constexpr (VB == 16)
+            reinterpret_cast<uint4 *>(dst)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+          else
+            st_v32(dst + i * 32, ld_v32(src + i * 32));
+        }
       }
     }
   }
-  if (blockIdx.x == 0) {
-    const char *s8 = jobs.src[j];
-    char *d8 = jobs.dst[j];
-    for (size_t i = nvec * 16 + threadIdx.x; i < bytes; i += kP2PThreads) d8[i] = s8[i];
-  }
+  if (blockIdx.x == 0)
+    for (size_t i = nvec * VB + threadIdx.x; i < bytes; i += kP2PThreads) dst[i] = src[i];
 }
 
 struct CeStreams {
@@ -156,15 +190,21 @@ extern "C" int cmb_p2p_enable_peer(int peer_device) {
   return CMB_OK;
 }
 
-extern "C" int cmb_p2p_scatter_store(void *const *dst, const void *const *src, const size_t *bytes,
-                                     int n, int ctas_per_job, cmb_stream_t stream) {
+namespace cmb {
+namespace {
+
+int scatter_store(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                  int ctas_per_job, int vec_bytes, cudaStream_t stream) {
   int rc = check_jobs("cmb_p2p_scatter_store", dst, src, bytes, n);
   if (rc) return rc;
+  if (vec_bytes != 16 && vec_bytes != 32)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_store: vec_bytes %d not 16 or 32", vec_bytes);
   Jobs jobs = {};
   size_t most = 0;
   for (int j = 0; j < n; ++j) {
-    if ((reinterpret_cast<uintptr_t>(dst[j]) | reinterpret_cast<uintptr_t>(src[j])) & 15)
-      return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_store: job %d not 16-byte aligned", j);
+    if ((reinterpret_cast<uintptr_t>(dst[j]) | reinterpret_cast<uintptr_t>(src[j])) & (vec_bytes - 1))
+      return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_store: job %d not %d-byte aligned", j,
+                  vec_bytes);
     jobs.src[j] = static_cast<const char *>(src[j]);
     jobs.dst[j] = static_cast<char *>(dst[j]);
     jobs.bytes[j] = bytes[j];
@@ -172,11 +212,33 @@ extern "C" int cmb_p2p_scatter_store(void *const *dst, const void *const *src, c
   }
   if (most == 0) return CMB_OK;
   if (ctas_per_job <= 0) ctas_per_job = (current_sm_count() * 2 + n - 1) / n;
-  size_t want = (most / 16 + kP2PThreads * 4 - 1) / (kP2PThreads * 4);
+  const size_t tile = (size_t)kP2PThreads * 4 * vec_bytes;
+  size_t want = (most + tile - 1) / tile;
   if ((size_t)ctas_per_job > want) ctas_per_job = static_cast<int>(want == 0 ? 1 : want);
-  k_p2p_store<<<dim3(ctas_per_job, n), kP2PThreads, 0, stream>>>(jobs);
+  if (vec_bytes == 16) k_p2p_store<16><<<dim3(ctas_per_job, n), kP2PThreads, 0, stream>>>(jobs);
+  else k_p2p_store<32><<<dim3(ctas_per_job, n), kP2PThreads, 0, stream>>>(jobs);
   CMB_LAUNCH_CHECK();
   return CMB_OK;
+}
+
+}  // namespace
+}  // namespace cmb
+
+extern "C" int cmb_p2p_scatter_store(void *const *dst, const void *const *src, const size_t *bytes,
+                                     int n, int ctas_per_job, cmb_stream_t stream) {
+  // 32-byte vectors when every job allows them
+  int vb = 32;
+  for (int j = 0; j < n && j < kMaxJobs; ++j)
+    if (dst != nullptr && src != nullptr &&
+        ((reinterpret_cast<uintptr_t>(dst[j]) | reinterpret_cast<uintptr_t>(src[j])) & 31))
+      vb = 16;
+  return scatter_store(dst, src, bytes, n, ctas_per_job, vb, stream);
+}
+
+extern "C" int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *src,
+                                           const size_t *bytes, int n, int ctas_per_job,
+                                           int vec_bytes, cmb_stream_t stream) {
+  return scatter_store(dst, src, bytes, n, ctas_per_job, vec_bytes, stream);
 }
 
 extern "C" int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src,

@@ -272,6 +272,11 @@ int cmb_p2p_enable_peer(int peer_device);
  * pointers; ctas_per_job <= 0 picks 2 * SMs / n. */
 int cmb_p2p_scatter_store(void *const *dst, const void *const *src, const size_t *bytes, int n,
                           int ctas_per_job, cmb_stream_t stream);
+/* cmb_p2p_scatter_store with an explicit vector width (16 or 32 bytes;
+ * pointers aligned to it), for sweeps.  cmb_p2p_scatter_store uses 32 when
+ * every job is 32-byte aligned. */
+int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *src, const size_t *bytes,
+                                int n, int ctas_per_job, int vec_bytes, cmb_stream_t stream);
 /* The same n copies by the copy engines (cudaMemcpyAsync, one internal
  * stream per job, joined back into `stream`). */
 int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src, const size_t *bytes,
