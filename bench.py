@@ -49,7 +49,7 @@ def log(*a):
 class Ranks:
     """Process-group plumbing: one process per GPU, launched by torchrun."""
 
-    def __init__(self, backend: str):
+    def __init__(self, backend: str, timeout_s: float = 120.0):
         import torch
         import torch.distributed as dist
 
@@ -62,7 +62,8 @@ class Ranks:
             import datetime
 
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+            dist.init_process_group(backend=backend,
+                                    timeout=datetime.timedelta(seconds=timeout_s))
 
     def barrier(self):
         if self.world > 1:

@@ -282,6 +282,14 @@ int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *src, const 
 int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src, const size_t *bytes,
                                 int n, cmb_stream_t stream);
 
+/* --- self-test of the bounded-wait rule -------------------------------- */
+
+/* One thread waits on an mbarrier phase that nothing completes, giving up
+ * after limit_ns (<= 2 s): *status (device) = CMB_ERR_TIMEOUT and
+ * *waited_ns (device) = how long it waited.  The device stays usable. */
+int cmb_selftest_wait_timeout(uint64_t limit_ns, int *status, uint64_t *waited_ns,
+                              cmb_stream_t stream);
+
 /* --- checks ---------------------------------------------------------- */
 
 /* *mismatches (device) = 0 iff a[0:bytes) == b[0:bytes) (otherwise the

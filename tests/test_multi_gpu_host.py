@@ -83,3 +83,41 @@ def test_rank_plumbing_two_gloo_processes():
         assert p.exitcode == 0
     for rank, mx, sm, hs in res:
         assert mx == 2.0 and sm == 3.0 and hs == [0, 1]
+
+
+def _dropper(rank, world, port, q):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
+                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank)})
+    import time
+
+    import bench
+
+    ranks = bench.Ranks("gloo", timeout_s=5.0)
+    ranks.barrier()
+    if rank == 1:
+        q.put((rank, "left"))
+        return  # leaves between steps, without its next collective
+    t0 = time.time()
+    try:
+        ranks.max(1.0)
+        q.put((rank, "no error"))
+    except Exception as e:  # the collective fails instead of hanging
+        q.put((rank, f"error after {time.time() - t0:.1f}s: {type(e).__name__}"))
+
+
+def test_peer_that_leaves_is_detected_by_timeout():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dropper, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
