@@ -42,6 +42,7 @@ SIGNATURES = {
     "cmb_chase_run": (_i, [_p, _sz, _u64, _u64, _i, _p, _p]),
     "cmb_chase_host_walk": (_i, [_p, _sz, _u64, _p]),
     "cmb_tma_tile_copy_bf16": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
+    "cmb_tma_tile_copy_tuned": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _p]),
     "cmb_tma_tile_load_bf16": (_i, [_p, _i, _i, _i, _i, _i, _p, _sz, _p, _p]),
     "cmb_tma_1d_latency": (_i, [_p, _sz, _i, _p, _p, _p]),
     "cmb_gemm_bf16": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),

@@ -228,6 +228,15 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, int32_t x, int32_
       : "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d_hint(const void *tmap, int32_t x, int32_t y,
+                                                  uint32_t src, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+      " [%0, {%1, %2}], [%3], %4;" ::"l"(tmap),
+      "r"(x), "r"(y), "r"(src), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -5,7 +5,8 @@
 // into a STAGES-deep shared-memory ring, each completion counted on the
 // stage's full mbarrier (expect_tx); a second thread (warp 1) stores each
 // tile back out with a tiled TMA store from the same buffer and hands the
-// stage back (empty mbarrier) once the store has finished reading it.
+// stage back (empty mbarrier) once the store has finished reading it; up to
+// STAGES / 2 stores read the ring at once.
 // Persistent grid: CTAs stride over the tile list.  In load-only mode (the
 // reference's G2S bandwidth probe, src/tma.cu:72-121) the second thread
 // only folds the first 16 bytes of each tile into a per-CTA XOR so the
@@ -72,7 +73,27 @@ constexpr int kTmaThreads = 64;  // warp 0: loads, warp 1: stores
 
 struct TileShape {
   int rows, cols, box_rows, box_cols, tiles_x, tiles;
+  int contiguous;  // 0: CTA b takes tiles b, b + grid, ...; 1: a contiguous run
+  int evict_first;  // 1: loads and stores carry an L2 evict-first policy
 };
+
+// k-th tile of this CTA and the number of tiles it owns.
+__device__ __forceinline__ int tile_of(const TileShape &s, int k) {
+  if (s.contiguous) {
+    const int per = (s.tiles + gridDim.x - 1) / gridDim.x;
+    return blockIdx.x * per + k;
+  }
+  return blockIdx.x + k * gridDim.x;
+}
+
+__device__ __forceinline__ int tiles_of(const TileShape &s) {
+  if (s.contiguous) {
+    const int per = (s.tiles + gridDim.x - 1) / gridDim.x;
+    const int first = blockIdx.x * per;
+    return first >= s.tiles ? 0 : min(per, s.tiles - first);
+  }
+  return blockIdx.x < s.tiles ? (s.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+}
 
 template <int STAGES, bool kStore>
 __global__ void __launch_bounds__(kTmaThreads, 1)
@@ -86,6 +107,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
   __shared__ int abort_flag, loads_issued, tiles_consumed;
 
+  // stores in flight per CTA: half the ring
+  constexpr int kLag = STAGES / 2 > 1 ? STAGES / 2 : 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -101,8 +124,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
   __syncthreads();
 
-  const int my_tiles =
-      blockIdx.x < shape.tiles ? (shape.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my_tiles = tiles_of(shape);
 
   if (warp == 0 && lane == 0) {
     // producer
@@ -115,12 +137,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         break;
       }
       if (*(volatile int *)&abort_flag) break;
-      const int t = blockIdx.x + k * gridDim.x;
+      const int t = tile_of(shape, k);
       const int ty = t / shape.tiles_x, tx = t - ty * shape.tiles_x;
       const uint32_t bar = dev::smem_addr(&full[s]);
       dev::mbar_arrive_expect_tx(bar, tile_bytes);
-      dev::tma_load_2d(dev::smem_addr(ring + (size_t)s * tile_bytes), &src_map,
-                       tx * shape.box_cols, ty * shape.box_rows, bar);
+      if (shape.evict_first)
+        dev::tma_load_2d_hint(dev::smem_addr(ring + (size_t)s * tile_bytes), &src_map,
+                              tx * shape.box_cols, ty * shape.box_rows, bar,
+                              dev::policy_evict_first());
+      else
+        dev::tma_load_2d(dev::smem_addr(ring + (size_t)s * tile_bytes), &src_map,
+                         tx * shape.box_cols, ty * shape.box_rows, bar);
     }
     loads_issued = k;
   } else if (warp == 1 && lane == 0) {
@@ -136,13 +163,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       }
       uint8_t *buf = ring + (size_t)s * tile_bytes;
       if (kStore) {
-        const int t = blockIdx.x + k * gridDim.x;
+        const int t = tile_of(shape, k);
         const int ty = t / shape.tiles_x, tx = t - ty * shape.tiles_x;
-        dev::tma_store_2d(&dst_map, tx * shape.box_cols, ty * shape.box_rows, dev::smem_addr(buf));
+        if (shape.evict_first)
+          dev::tma_store_2d_hint(&dst_map, tx * shape.box_cols, ty * shape.box_rows,
+                                 dev::smem_addr(buf), dev::policy_evict_first());
+        else
+          dev::tma_store_2d(&dst_map, tx * shape.box_cols, ty * shape.box_rows,
+                            dev::smem_addr(buf));
         dev::bulk_commit_group();
-        // The store of tile k-1 has finished reading its stage.
-        dev::bulk_wait_group_read<1>();
-        if (k > 0) dev::mbar_arrive(dev::smem_addr(&empty[(k - 1) % STAGES]));
+        // Keep kLag stores reading shared memory at once: once only kLag
+        // are pending, the store of tile k - kLag has read its stage.
+        dev::bulk_wait_group_read<kLag>();
+        if (k >= kLag) dev::mbar_arrive(dev::smem_addr(&empty[(k - kLag) % STAGES]));
       } else {
         const uint4 v = *reinterpret_cast<const uint4 *>(buf);
         x ^= v.x ^ v.y ^ v.z ^ v.w;
@@ -209,7 +242,7 @@ int launch_tile(const CUtensorMap &sm, const CUtensorMap &dm, TileShape shape, u
 
 int tile_impl(void *dst, const void *src, int rows, int cols, int box_rows, int box_cols,
               int stages, int ctas_per_sm, int *status, uint32_t *xor_out, int grid_override,
-              cmb_stream_t stream) {
+              int contiguous, cmb_stream_t stream) {
   const bool store = dst != nullptr;
   if (src == nullptr) return fail(CMB_ERR_INVALID_ARG, "tma tile: null src");
   if (rows <= 0 || cols <= 0) return fail(CMB_ERR_INVALID_ARG, "tma tile: empty matrix");
@@ -247,6 +280,8 @@ int tile_impl(void *dst, const void *src, int rows, int cols, int box_rows, int 
   const long long tiles = (long long)shape.tiles_x * ((rows + box_rows - 1) / box_rows);
   if (tiles > 0x7fffffffLL) return fail(CMB_ERR_INVALID_ARG, "tma tile: too many tiles");
   shape.tiles = static_cast<int>(tiles);
+  shape.contiguous = (contiguous & 1) ? 1 : 0;
+  shape.evict_first = (contiguous & 2) ? 1 : 0;
   int grid = grid_override > 0 ? grid_override : current_sm_count() * ctas_per_sm;
   if (grid > shape.tiles) grid = shape.tiles;
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
@@ -280,7 +315,15 @@ extern "C" int cmb_tma_tile_copy_bf16(void *dst, const void *src, int rows, int 
                                       int *status, cmb_stream_t stream) {
   if (dst == nullptr) return fail(CMB_ERR_INVALID_ARG, "cmb_tma_tile_copy_bf16: null dst");
   return tile_impl(dst, src, rows, cols, box_rows, box_cols, stages, ctas_per_sm, status, nullptr,
-                   0, stream);
+                   0, 0, stream);
+}
+
+extern "C" int cmb_tma_tile_copy_tuned(void *dst, const void *src, int rows, int cols,
+                                       int box_rows, int box_cols, int stages, int ctas_per_sm,
+                                       int flags, int *status, cmb_stream_t stream) {
+  if (dst == nullptr) return fail(CMB_ERR_INVALID_ARG, "cmb_tma_tile_copy_tuned: null dst");
+  return tile_impl(dst, src, rows, cols, box_rows, box_cols, stages, ctas_per_sm, status, nullptr,
+                   0, flags, stream);
 }
 
 extern "C" int cmb_tma_tile_load_bf16(const void *src, int rows, int cols, int box_rows,
@@ -292,7 +335,7 @@ extern "C" int cmb_tma_tile_load_bf16(const void *src, int rows, int cols, int b
   if ((size_t)grid > xor_words) grid = static_cast<int>(xor_words);
   CMB_CUDA_TRY(cudaMemsetAsync(xor_out, 0, xor_words * sizeof(uint32_t), stream));
   return tile_impl(nullptr, src, rows, cols, box_rows, box_cols, stages, 1, status, xor_out, grid,
-                   stream);
+                   0, stream);
 }
 
 extern "C" int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint32_t *out_cycles,

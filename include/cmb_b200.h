@@ -165,6 +165,13 @@ int cmb_chase_host_walk(const uint32_t *host_links, size_t words, uint64_t hops,
 int cmb_tma_tile_copy_bf16(void *dst, const void *src, int rows, int cols, int box_rows,
                            int box_cols, int stages, int ctas_per_sm, int *status,
                            cmb_stream_t stream);
+/* cmb_tma_tile_copy_bf16 with placement options, for sweeps: flags bit 0 =
+ * give each CTA one contiguous run of tiles (default: CTA b strides over
+ * tiles b, b + grid, ... in row-major tile order); bit 1 = L2 evict-first
+ * policy on the loads and stores. */
+int cmb_tma_tile_copy_tuned(void *dst, const void *src, int rows, int cols, int box_rows,
+                            int box_cols, int stages, int ctas_per_sm, int flags, int *status,
+                            cmb_stream_t stream);
 /* Load-only form of the same pipeline (the reference's read-only G2S
  * bandwidth, src/tma.cu:72-121,247): one CTA per SM (at most xor_words);
  * CTA b writes to xor_out[b] the XOR of the first four 32-bit words of every
