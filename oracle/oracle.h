@@ -8,17 +8,20 @@
  *
  * Parity status against the reference:
  *   - hash fill: restates the reference formula (src/mem_global.cu:7-10,
- *     include/memory_chase.h:128-133).
+ *     include/memory_chase.h:128-133); pinned to the output of the
+ *     reference's kernel_init_stream run on a B200.
  *   - chase endpoint: the reference's only self-check
  *     (include/memory_chase.h:152-153,161-164) is the walk restated in
- *     orc_chase_walk().
+ *     orc_chase_walk(); pinned to the endpoints of the reference's
+ *     kernel_random_chase_cg run on a B200 over orc_chase_build's array.
  *   - stream sum, copy, TMA tile copy, GEMM: the reference pins no result for
  *     these (its outputs are XOR sinks, one smem byte, or sums of constants),
  *     so these restatements are parity unpinned against the reference; tests
  *     check them through size-independent properties (identity, fp64
  *     re-summation, fp64 GEMM on sampled tiles).
- * Which of these the committed golden fixtures pin is stated in
- * tests/golden/make_golden.py.
+ * The fixtures and the scripts that made them are in tests/golden/
+ * (make_golden.py: the reference's result logger; make_ref_fixtures.py: the
+ * reference's kernels built for sm_100a by this directory's Makefile).
  */
 #ifndef CMB_ORACLE_H
 #define CMB_ORACLE_H
