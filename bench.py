@@ -279,6 +279,8 @@ def run_ours(args) -> int:
     }
     if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_memcpy_baseline(1 << 30, 8, 1)
+        if not args.no_probes:
+            result["cpu_baseline"]["probes"] = cpu_probe_baselines()
     del src, dst
     torch.cuda.empty_cache()
     if not args.no_probes:
@@ -586,6 +588,47 @@ def run_probe_only(args) -> int:
         torch.cuda.empty_cache()
     print(json.dumps({"probes": out}), flush=True)
     return 0
+
+
+def cpu_probe_baselines() -> dict:
+    """The host reference of the other probes, timed on this box's cores on
+    bounded samples (the oracle: threaded fp64 sum, the serial chase walk,
+    threaded blocked fp32 GEMM rows)."""
+    import numpy as np
+
+    import oracle
+
+    orc = oracle.load()
+    threads = orc.orc_hw_threads()
+    out = {"cores": threads}
+    n = 1 << 28
+    x = np.empty(n, np.float32)
+    orc.orc_fill_uniform_f32(oracle.ptr(x), n, SEED)
+    t0 = time.perf_counter()
+    orc.orc_sum_f64(oracle.ptr(x), n, threads)
+    dt = time.perf_counter() - t0
+    out["sum_1gib"] = {"GB/s": round(4.0 * n / dt / 1e9, 2), "threads": threads,
+                       "sample": "fp64 sum of fp32[2^28]"}
+    del x
+    links = np.empty((512 << 20) // 4, np.uint32)
+    orc.orc_chase_build(oracle.ptr(links), links.nbytes, 0xC0DA)
+    hops = 1 << 22
+    t0 = time.perf_counter()
+    orc.orc_chase_walk(oracle.ptr(links), hops, 0)
+    dt = time.perf_counter() - t0
+    out["chase_512mib"] = {"ns_per_hop": round(dt * 1e9 / hops, 2), "threads": 1,
+                           "sample": "serial walk, 2^22 hops over 512 MiB"}
+    del links
+    K, N, rows = 8192, 8192, 16 * threads
+    a = np.random.default_rng(0).integers(0, 1 << 16, rows * K, dtype=np.uint16) & 0x3FFF
+    b = np.random.default_rng(1).integers(0, 1 << 16, N * K, dtype=np.uint16) & 0x3FFF
+    c = np.empty(rows * N, np.float32)
+    t0 = time.perf_counter()
+    orc.orc_gemm_bf16_rows_f32(oracle.ptr(a), oracle.ptr(b), oracle.ptr(c), N, K, 0, rows, threads)
+    dt = time.perf_counter() - t0
+    out["gemm_bf16"] = {"TFLOP/s": round(2.0 * rows * N * K / dt / 1e12, 5), "threads": threads,
+                        "sample": f"{rows} rows of an 8192^3 bf16 GEMM (blocked fp32)"}
+    return out
 
 
 def run_probes(args, ranks, peaks) -> dict:

@@ -315,32 +315,37 @@ typedef struct {
 
 static void *gemm_worker(void *p) {
   gemm_job *g = (gemm_job *)p;
-  const int KB = 256;
+  /* B is decoded in blocks of KB x 64, stored k-major, so the inner loop
+   * is an axpy over 64 output columns (vectorisable without reassociating
+   * any sum: each output column accumulates in k order). */
+  const int KB = 256, CB = 64;
+  float *bt = (float *)malloc(sizeof(float) * KB * CB);
   float *a = (float *)malloc(sizeof(float) * KB);
-  float *b = (float *)malloc(sizeof(float) * KB * 64);
   for (int r = g->r0; r < g->r1; ++r)
     for (int c = 0; c < g->N; ++c) g->C[(size_t)r * g->N + c] = 0.0f;
   for (int k0 = 0; k0 < g->K; k0 += KB) {
     int kb = g->K - k0 < KB ? g->K - k0 : KB;
-    for (int c0 = 0; c0 < g->N; c0 += 64) {
-      int cb = g->N - c0 < 64 ? g->N - c0 : 64;
+    for (int c0 = 0; c0 < g->N; c0 += CB) {
+      int cb = g->N - c0 < CB ? g->N - c0 : CB;
       for (int c = 0; c < cb; ++c)
         for (int k = 0; k < kb; ++k)
-          b[c * KB + k] = orc_bf16_to_f32(g->B[(size_t)(c0 + c) * g->K + k0 + k]);
+          bt[k * CB + c] = orc_bf16_to_f32(g->B[(size_t)(c0 + c) * g->K + k0 + k]);
       for (int r = g->r0; r < g->r1; ++r) {
         for (int k = 0; k < kb; ++k) a[k] = orc_bf16_to_f32(g->A[(size_t)r * g->K + k0 + k]);
-        float *crow = g->C + (size_t)r * g->N + c0;
-        for (int c = 0; c < cb; ++c) {
-          const float *bc = b + c * KB;
-          float s = 0.0f;
-          for (int k = 0; k < kb; ++k) s += a[k] * bc[k];
-          crow[c] += s;
+        float acc[64];
+        for (int c = 0; c < CB; ++c) acc[c] = 0.0f;
+        for (int k = 0; k < kb; ++k) {
+          const float av = a[k];
+          const float *brow = bt + k * CB;
+          for (int c = 0; c < CB; ++c) acc[c] += av * brow[c];
         }
+        float *crow = g->C + (size_t)r * g->N + c0;
+        for (int c = 0; c < cb; ++c) crow[c] += acc[c];
       }
     }
   }
   free(a);
-  free(b);
+  free(bt);
   return NULL;
 }
 
