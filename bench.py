@@ -619,9 +619,11 @@ def cpu_probe_baselines() -> dict:
     out["chase_512mib"] = {"ns_per_hop": round(dt * 1e9 / hops, 2), "threads": 1,
                            "sample": "serial walk, 2^22 hops over 512 MiB"}
     del links
-    K, N, rows = 8192, 8192, 16 * threads
-    a = np.random.default_rng(0).integers(0, 1 << 16, rows * K, dtype=np.uint16) & 0x3FFF
-    b = np.random.default_rng(1).integers(0, 1 << 16, N * K, dtype=np.uint16) & 0x3FFF
+    K, N, rows = 8192, 8192, 64 * threads
+    # N(0, 1/K) operands, as the GPU probe fills them, truncated to bf16
+    bf16 = lambda x: (x.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    a = bf16(np.random.default_rng(0).standard_normal(rows * K, np.float32) * K ** -0.5)
+    b = bf16(np.random.default_rng(1).standard_normal(N * K, np.float32) * K ** -0.5)
     c = np.empty(rows * N, np.float32)
     t0 = time.perf_counter()
     orc.orc_gemm_bf16_rows_f32(oracle.ptr(a), oracle.ptr(b), oracle.ptr(c), N, K, 0, rows, threads)

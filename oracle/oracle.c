@@ -206,7 +206,8 @@ double orc_memcpy_mt(void *dst, const void *src, size_t n, int threads) {
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 
-float orc_bf16_to_f32(uint16_t v) { return u2f((uint32_t)v << 16); }
+static inline float bf16_to_f32(uint16_t v) { return u2f((uint32_t)v << 16); }
+float orc_bf16_to_f32(uint16_t v) { return bf16_to_f32(v); }
 
 uint16_t orc_f32_to_bf16_rne(float f) {
   uint32_t u = f2u(f);
@@ -310,37 +311,55 @@ void orc_gemm_tile_f64(const void *A, const void *B, int dtype, int K, int lda,
 typedef struct {
   const uint16_t *A, *B;
   float *C;
-  int N, K, r0, r1;
+  int N, K, row0, rows, c_lo, c_hi;
 } gemm_job;
 
+/* One thread owns the output columns [c_lo, c_hi) of every sampled row, so
+ * each B element is decoded once in total.  B is decoded in blocks of
+ * KB x 64, stored k-major; the inner loop is an axpy over 64 output columns
+ * for four rows at once (each output accumulates in k order, no sum is
+ * reassociated).  Built for several ISA levels (ifunc dispatch at load time)
+ * so the timed baseline uses the host's vector width without tying the build
+ * to it. */
+__attribute__((target_clones("arch=x86-64-v4", "arch=x86-64-v3", "default")))
 static void *gemm_worker(void *p) {
   gemm_job *g = (gemm_job *)p;
-  /* B is decoded in blocks of KB x 64, stored k-major, so the inner loop
-   * is an axpy over 64 output columns (vectorisable without reassociating
-   * any sum: each output column accumulates in k order). */
-  const int KB = 256, CB = 64;
+  enum { KB = 256, CB = 64, RB = 4 };
   float *bt = (float *)malloc(sizeof(float) * KB * CB);
-  float *a = (float *)malloc(sizeof(float) * KB);
-  for (int r = g->r0; r < g->r1; ++r)
-    for (int c = 0; c < g->N; ++c) g->C[(size_t)r * g->N + c] = 0.0f;
+  float *a = (float *)malloc(sizeof(float) * KB * RB);
+  for (int r = 0; r < g->rows; ++r)
+    for (int c = g->c_lo; c < g->c_hi; ++c) g->C[(size_t)r * g->N + c] = 0.0f;
   for (int k0 = 0; k0 < g->K; k0 += KB) {
-    int kb = g->K - k0 < KB ? g->K - k0 : KB;
-    for (int c0 = 0; c0 < g->N; c0 += CB) {
-      int cb = g->N - c0 < CB ? g->N - c0 : CB;
-      for (int c = 0; c < cb; ++c)
+    const int kb = g->K - k0 < KB ? g->K - k0 : KB;
+    for (int c0 = g->c_lo; c0 < g->c_hi; c0 += CB) {
+      const int cb = g->c_hi - c0 < CB ? g->c_hi - c0 : CB;
+      for (int c = 0; c < CB; ++c)
         for (int k = 0; k < kb; ++k)
-          bt[k * CB + c] = orc_bf16_to_f32(g->B[(size_t)(c0 + c) * g->K + k0 + k]);
-      for (int r = g->r0; r < g->r1; ++r) {
-        for (int k = 0; k < kb; ++k) a[k] = orc_bf16_to_f32(g->A[(size_t)r * g->K + k0 + k]);
-        float acc[64];
-        for (int c = 0; c < CB; ++c) acc[c] = 0.0f;
+          bt[k * CB + c] = c < cb ? bf16_to_f32(g->B[(size_t)(c0 + c) * g->K + k0 + k]) : 0.0f;
+      for (int r0 = 0; r0 < g->rows; r0 += RB) {
+        const int rb = g->rows - r0 < RB ? g->rows - r0 : RB;
+        for (int q = 0; q < RB; ++q)
+          for (int k = 0; k < kb; ++k)
+            a[q * KB + k] = q < rb ? bf16_to_f32(g->A[(size_t)(g->row0 + r0 + q) * g->K + k0 + k])
+                                   : 0.0f;
+        float acc[RB][CB];
+        for (int q = 0; q < RB; ++q)
+          for (int c = 0; c < CB; ++c) acc[q][c] = 0.0f;
         for (int k = 0; k < kb; ++k) {
-          const float av = a[k];
           const float *brow = bt + k * CB;
-          for (int c = 0; c < CB; ++c) acc[c] += av * brow[c];
+          const float a0 = a[k], a1 = a[KB + k], a2 = a[2 * KB + k], a3 = a[3 * KB + k];
+          for (int c = 0; c < CB; ++c) {
+            const float b = brow[c];
+            acc[0][c] += a0 * b;
+            acc[1][c] += a1 * b;
+            acc[2][c] += a2 * b;
+            acc[3][c] += a3 * b;
+          }
         }
-        float *crow = g->C + (size_t)r * g->N + c0;
-        for (int c = 0; c < cb; ++c) crow[c] += acc[c];
+        for (int q = 0; q < rb; ++q) {
+          float *crow = g->C + (size_t)(r0 + q) * g->N + c0;
+          for (int c = 0; c < cb; ++c) crow[c] += acc[q][c];
+        }
       }
     }
   }
@@ -352,17 +371,17 @@ static void *gemm_worker(void *p) {
 void orc_gemm_bf16_rows_f32(const uint16_t *A, const uint16_t *B, float *C,
                             int N, int K, int row0, int rows, int threads) {
   int t = pick_threads(threads);
-  if (t > rows) t = rows > 0 ? rows : 1;
+  const int blocks = (N + 63) / 64; /* column blocks of 64 */
+  if (t > blocks) t = blocks > 0 ? blocks : 1;
   pthread_t th[256];
   gemm_job jobs[256];
-  int per = (rows + t - 1) / t;
   int used = 0;
   for (int k = 0; k < t; ++k) {
-    int a = row0 + k * per, b = row0 + (k + 1) * per;
-    if (a >= row0 + rows) break;
-    if (b > row0 + rows) b = row0 + rows;
-    jobs[k] = (gemm_job){A, B, C, N, K, a, b};
-    pthread_create(&th[k], NULL, gemm_worker, &jobs[k]);
+    int lo = (int)((long)blocks * k / t) * 64, hi = (int)((long)blocks * (k + 1) / t) * 64;
+    if (hi > N) hi = N;
+    if (lo >= hi) continue;
+    jobs[used] = (gemm_job){A, B, C, N, K, row0, rows, lo, hi};
+    pthread_create(&th[used], NULL, gemm_worker, &jobs[used]);
     ++used;
   }
   for (int k = 0; k < used; ++k) pthread_join(th[k], NULL);

@@ -87,7 +87,8 @@ void orc_gemm_tile_f64(const void *A, const void *B, int dtype, int K,
                        int lda, int ldb, int row0, int col0, int tm, int tn,
                        double scale_a, double scale_b, double *out);
 /* Blocked fp32 GEMM over host threads (the CPU baseline's timed kernel);
- * computes rows [row0, row0 + rows) of C = A * B^T for bf16 A, B. */
+ * computes rows [row0, row0 + rows) of C = A * B^T for bf16 A, B, written
+ * as a rows x N row-major block at C.  Threads split the output columns. */
 void orc_gemm_bf16_rows_f32(const uint16_t *A, const uint16_t *B, float *C,
                             int N, int K, int row0, int rows, int threads);
 
