@@ -64,6 +64,7 @@ def load():
 
 
 def ptr(array) -> int:
-    """Address of a C-contiguous numpy array."""
+    """Address of a C-contiguous numpy array.  The caller keeps the array
+    alive (bound to a name) for as long as the address is used."""
     assert array.flags["C_CONTIGUOUS"]
     return array.ctypes.data

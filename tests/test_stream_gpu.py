@@ -100,7 +100,8 @@ def test_sum_matches_oracle(cuda, cmb, orc, n, offset):
     orc.orc_fill_uniform_f32(ptr(host), host.size, 11)
     d = cuda.from_numpy(host).cuda()
     got = _sum(cuda, cmb, d, n=n, offset_elems=offset)
-    ref = orc.orc_sum_f64(ptr(host[offset:offset + n].copy()), n, 0) if n else 0.0
+    part = host[offset:offset + n].copy()  # named: ptr() does not keep the array alive
+    ref = orc.orc_sum_f64(ptr(part), n, 0) if n else 0.0
     assert abs(got - ref) <= REL_TOL_SUM * max(abs(ref), 1e-30) or abs(got - ref) < 1e-9
 
 
