@@ -339,10 +339,19 @@ def _time_launches(torch, stream, fn, reps):
     return [evs[k].elapsed_time(evs[k + 1]) for k in range(reps)]
 
 
+def _median_ms(torch, stream, fn, reps=9, warm=3):
+    """Median device time (ms) of `reps` back-to-back launches after `warm`
+    untimed ones (clocks and TLBs settle in the warm-up)."""
+    for _ in range(warm):
+        fn()
+    return statistics.median(_time_launches(torch, stream, fn, reps))
+
+
 def probe_stream_1gib(torch, stream, sh, peaks):
     """Config: fp32[2^28] (1 GiB) copy (bit-exact) and sum (checked against
-    an fp64 sum, rel 1e-5); median of 5 timed launches after one warm-up, as
-    the reference's measure() (src/mem_global.cu:42-53)."""
+    an fp64 sum, rel 1e-5); median of 9 timed launches after 3 warm-up
+    launches (the reference's measure() takes the median of 5 after one
+    warm-up, src/mem_global.cu:42-53)."""
     from cuda_micro_bench_b200 import check, lib
 
     n = 1 << 28
@@ -357,8 +366,8 @@ def probe_stream_1gib(torch, stream, sh, peaks):
     ssum = lambda: check("cmb_stream_sum_f32", ctypes.c_void_p(src.data_ptr()), n,
                          ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
                          ws_bytes, sh)
-    copy_ms = statistics.median(_time_launches(torch, stream, copy, 6)[1:])
-    sum_ms = statistics.median(_time_launches(torch, stream, ssum, 6)[1:])
+    copy_ms = _median_ms(torch, stream, copy)
+    sum_ms = _median_ms(torch, stream, ssum)
     copy_ok = bool(torch.equal(src.view(torch.int32), dst.view(torch.int32)))
     ref = float(src.double().sum().item())  # fp64 check sum
     got = float(out.item())
@@ -423,7 +432,7 @@ def probe_tma(torch, stream, sh, peaks):
         fn = lambda: check("cmb_tma_tile_copy_bf16", ctypes.c_void_p(dst.data_ptr()),
                            ctypes.c_void_p(src.data_ptr()), n, n, 128, 128, stages, ctas,
                            ctypes.c_void_p(status.data_ptr()), sh)
-        ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+        ms = _median_ms(torch, stream, fn)
         gbs = 2.0 * 2 * n * n / (ms * 1e-3) / 1e9
         out[label] = {"GB/s": round(gbs, 2), "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
                       "frac_of_8tbs_spec": round(gbs / 8000.0, 4), "stages": stages, "box": [128, 128],
@@ -432,7 +441,7 @@ def probe_tma(torch, stream, sh, peaks):
     fn = lambda: check("cmb_tma_tile_load_bf16", ctypes.c_void_p(src.data_ptr()), n, n, 128, 128,
                        4, ctypes.c_void_p(xor.data_ptr()), 4096,
                        ctypes.c_void_p(status.data_ptr()), sh)
-    ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+    ms = _median_ms(torch, stream, fn)
     gbs = 2.0 * n * n / (ms * 1e-3) / 1e9
     out["load_only_4stage"] = {"GB/s": round(gbs, 2), "GiB/s": round(gbs / 1.073741824, 2),
                                "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
@@ -492,7 +501,7 @@ def probe_gemm(torch, stream, sh, peaks):
         fn = lambda: check("cmb_gemm_bf16", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
                            ctypes.c_void_p(C.data_ptr()), M, N, K, cg,
                            ctypes.c_void_p(status.data_ptr()), sh)
-        ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+        ms = _median_ms(torch, stream, fn)
         tf = flop / (ms * 1e-3) / 1e12
         err = sampled_err(a64, b64)
         out[label] = {"TFLOP/s": round(tf, 1), "frac_of_measured_bf16": round(tf / peaks["bf16_tflops"], 4),
@@ -509,7 +518,7 @@ def probe_gemm(torch, stream, sh, peaks):
         fn = lambda: check("cmb_gemm_e4m3", ctypes.c_void_p(qa.data_ptr()), ctypes.c_void_p(qb.data_ptr()),
                            ctypes.c_void_p(C.data_ptr()), M, N, K, ctypes.c_void_p(sa.data_ptr()),
                            ctypes.c_void_p(sb.data_ptr()), cg, ctypes.c_void_p(status.data_ptr()), sh)
-        ms = statistics.median(_time_launches(torch, stream, fn, 6)[1:])
+        ms = _median_ms(torch, stream, fn)
         tf = flop / (ms * 1e-3) / 1e12
         err = sampled_err(a8, b8)
         out[label] = {"TFLOP/s": round(tf, 1), "frac_of_4500_spec": round(tf / 4500.0, 4),
