@@ -458,9 +458,13 @@ def probe_tma(torch, stream, sh, peaks):
 
 def probe_gemm(torch, stream, sh, peaks):
     """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5, fp32 accumulation in
-    TMEM, 2-CTA tiles of 256 x 512 (two N=256 accumulators per pair), and the
-    1-CTA 128x256 form; FP8 e4m3 with a per-tensor scale.  TFLOP/s = 2*M*N*K / median launch time; 8 sampled
-    64x64 output tiles are checked against an fp64 product."""
+    TMEM, 2-CTA tiles of 256 x 512 (two N=256 accumulators per pair, held
+    8-warp epilogue), and the 1-CTA 128x256 form; FP8 e4m3 with a per-tensor
+    scale.  TFLOP/s = 2*M*N*K / median launch time; 8 sampled 64x64 output
+    tiles are checked against an fp64 product.  cuBLAS (torch.mm /
+    torch._scaled_mm) on the same operands with the same fp32 output is
+    timed alongside as a live reference point; it is not part of the
+    product."""
     from cuda_micro_bench_b200 import check
 
     M = N = K = 8192
@@ -525,7 +529,28 @@ def probe_gemm(torch, stream, sh, peaks):
                       "frac_of_2x_measured_bf16": round(tf / (2 * peaks["bf16_tflops"]), 4),
                       "ms": round(ms, 4), "sampled_tiles_max_rel_err": err,
                       "within_1e-2": err <= 1e-2, "status": int(status.item())}
-    del A, B, C, qa, qb, a8, b8
+    del a8, b8
+    # cuBLAS on the same operands, fp32 output like the kernels above
+    a16, b16 = A.view(M, K).view(torch.bfloat16), B.view(N, K).view(torch.bfloat16)
+    f8a, f8b = qa.view(M, K).view(torch.float8_e4m3fn), qb.view(N, K).view(torch.float8_e4m3fn)
+    live = {}
+    try:
+        ms = _median_ms(torch, stream, lambda: torch.mm(a16, b16.t(), out_dtype=torch.float32))
+        live["bf16_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+        ms = _median_ms(torch, stream, lambda: torch._scaled_mm(
+            f8a, f8b.t(), scale_a=sa[0], scale_b=sb[0], out_dtype=torch.float32))
+        live["e4m3_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+    except (RuntimeError, TypeError) as e:  # an older torch without these forms
+        live["error"] = str(e).splitlines()[0][:200]
+    if "bf16_TFLOP/s" in live:
+        out["bf16_8192_2cta"]["frac_of_live_cublas"] = round(
+            out["bf16_8192_2cta"]["TFLOP/s"] / live["bf16_TFLOP/s"], 4)
+    if "e4m3_TFLOP/s" in live:
+        out["fp8_e4m3_8192_2cta"]["frac_of_live_cublas"] = round(
+            out["fp8_e4m3_8192_2cta"]["TFLOP/s"] / live["e4m3_TFLOP/s"], 4)
+    live["what"] = "torch.mm / torch._scaled_mm (cuBLASLt), same operands, fp32 C, timed alongside"
+    out["cublas_same_operands"] = live
+    del A, B, C, qa, qb, a16, b16, f8a, f8b
     return out
 
 

@@ -6,7 +6,8 @@
 // C[M x N] (fp32, row-major) = scale * A[M x K] * B[N x K]^T, A and B
 // K-major ("row.col", src/tensor_core_extended.cu:116).
 //
-// Structure (one CTA per SM, persistent, 192 threads):
+// Structure (one CTA per SM, persistent, 192 threads; 320 with the held
+// epilogue below):
 //   warp 0      TMA producer: 128-byte-swizzled K-major tiles of A and B
 //               into a STAGES-deep shared-memory ring (full/empty mbarriers)
 //   warp 1      TMEM allocator and MMA issuer: one thread issues
@@ -26,9 +27,13 @@
 //   CTAs complete on CTA 0's full barrier, and CTA 0 commits to both CTAs'
 //   barriers one address at a time.  NSUB = 2 (the default) issues two MMAs
 //   per K slice into all 512 TMEM columns: a quarter fewer bytes loaded per
-//   FLOP than 256 x 256 tiles, at the cost of the epilogue no longer
-//   overlapping the next tile's MMAs (on B200 the load savings win: ~1.5
-//   PFLOP/s bf16 against ~1.2 for 256 x 256).
+//   FLOP than 256 x 256 tiles (on B200 the load savings win: ~1.5 PFLOP/s
+//   bf16 against ~1.2 for 256 x 256), but no second accumulator for the
+//   epilogue to drain while the next tile runs.  With 8 epilogue warps the
+//   drain is split instead: each warp loads 128 columns of one N=256 half
+//   into registers and hands that half back before storing it, and the MMA
+//   issuer starts the next tile on half 0 over the stages already loaded
+//   while half 1 drains ("held" epilogue).
 // All waits are bounded; a wait that gives up reports CMB_ERR_TIMEOUT in
 // `status` and every role drains and leaves.
 #include <cuda.h>
@@ -48,7 +53,6 @@ namespace {
 
 template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW>
 struct GemmCfg {
-  static constexpr int kEpiWarps = EPIW;             // epilogue warps: 4 or 8
   static constexpr int kThreads = 64 + 32 * EPIW;
   static constexpr int kBmCta = 128;                 // A rows per CTA
   static constexpr int kBn = 256;                    // MMA N
@@ -68,9 +72,15 @@ struct GemmCfg {
   // 256-column tiles keep two accumulators (the epilogue of one tile
   // overlaps the MMAs of the next); 512-column tiles use all 512 columns.
   static constexpr int kAccBufs = 2 / NSUB;
-  // TMA-store epilogue: per epilogue warp two 32 x 32 fp32 staging boxes.
+  // 512-column tiles with 8 epilogue warps drain each N=256 half of the
+  // accumulator through registers (128 columns per warp) and hand that half
+  // back before storing it, so the next tile's MMAs into it can start.
+  static constexpr bool kHeld = NSUB == 2 && EPIW == 8;
+  // TMA-store epilogue: 32 x 32 fp32 staging boxes, two per warp (one in the
+  // held mode, which keeps its data in registers instead).
   static constexpr int kEpiBoxBytes = 32 * 32 * 4;
-  static constexpr int kEpiBytes = kTmaEpi ? EPIW * 2 * kEpiBoxBytes : 0;
+  static constexpr int kEpiBoxes = kHeld ? 1 : 2;
+  static constexpr int kEpiBytes = kTmaEpi ? EPIW * kEpiBoxes * kEpiBoxBytes : 0;
   static constexpr size_t kSmem = (size_t)kStages * kStageBytes + kEpiBytes + 1024;
   static constexpr uint32_t kIdesc = tc::instr_desc<kTileM, kBn, kFp8>();
 };
@@ -189,7 +199,88 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
+    if (lane == 0 && rank == 0 && Cfg::kHeld) {
+      // ------------------------------------------- MMA issuer, held epilogue
+      // The two N=256 halves of the accumulator come back from the epilogue
+      // one after the other.  Each tile starts with the MMAs of half 0 over
+      // every stage already in the ring, then waits for half 1, issues its
+      // MMAs over the same stages and frees them; the rest of K runs both
+      // halves per stage.  Each half still accumulates in K order.
+      int it = 0, j = 0;
+      bool ok = true;
+      const int pre = kblocks < Cfg::kStages ? kblocks : Cfg::kStages;
+      for (int t = cluster; t < tiles && ok; t += nclusters, ++j) {
+        const uint32_t aph = static_cast<uint32_t>(j) & 1;
+        for (int u = 0; u < 2 && ok; ++u) {
+          if (!dev::mbar_wait_bounded(dev::smem_addr(&tempty[u]), aph ^ 1) ||
+              *(volatile int *)&abort_flag) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          for (int kb = 0; kb < pre; ++kb) {
+            const int s = (it + kb) % Cfg::kStages;
+            const uint32_t ph = ((it + kb) / Cfg::kStages) & 1;
+            if (u == 0) {
+              if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), ph) ||
+                  *(volatile int *)&abort_flag) {
+                ok = false;
+                break;
+              }
+              tc::fence_after_sync();
+            }
+            const uint32_t a_addr = dev::smem_addr(ring + (size_t)s * Cfg::kStageBytes);
+            const uint64_t da = tc::sw128_kmajor_desc(a_addr);
+            const uint64_t db = tc::sw128_kmajor_desc(a_addr + Cfg::kABytes);
+#pragma unroll
+            for (int k = 0; k < Cfg::kMmaPerStage; ++k)
+              tc::mma<CG, kFp8>(tmem_base + u * Cfg::kBn, da + 2 * k,
+                                db + (u * Cfg::kBSubBytes >> 4) + 2 * k, Cfg::kIdesc,
+                                (kb | k) != 0 ? 1u : 0u);
+            if (u == 1) {
+              const uint32_t eb = dev::smem_addr(&empty[s]);
+              tc::commit<CG>(eb);
+              if constexpr (CG == 2) tc::commit<CG>(tc::map_to_cta(eb, 1));
+            }
+          }
+        }
+        if (!ok) break;
+        it += pre;
+        for (int kb = pre; kb < kblocks; ++kb, ++it) {
+          const int s = it % Cfg::kStages;
+          const uint32_t ph = (it / Cfg::kStages) & 1;
+          if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), ph) ||
+              *(volatile int *)&abort_flag) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t a_addr = dev::smem_addr(ring + (size_t)s * Cfg::kStageBytes);
+          const uint64_t da = tc::sw128_kmajor_desc(a_addr);
+          const uint64_t db = tc::sw128_kmajor_desc(a_addr + Cfg::kABytes);
+#pragma unroll
+          for (int k = 0; k < Cfg::kMmaPerStage; ++k)
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+              tc::mma<CG, kFp8>(tmem_base + u * Cfg::kBn, da + 2 * k,
+                                db + (u * Cfg::kBSubBytes >> 4) + 2 * k, Cfg::kIdesc, 1u);
+          const uint32_t eb = dev::smem_addr(&empty[s]);
+          tc::commit<CG>(eb);
+          if constexpr (CG == 2) tc::commit<CG>(tc::map_to_cta(eb, 1));
+        }
+        if (!ok) break;
+        const uint32_t fb = dev::smem_addr(&tfull[0]);
+        tc::commit<CG>(fb);
+        if constexpr (CG == 2) tc::commit<CG>(tc::map_to_cta(fb, 1));
+      }
+      if (!ok) {
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+        atomicExch(&abort_flag, 1);
+      }
+      tc::commit<CG>(dev::smem_addr(&mma_done));
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&mma_done), 0))
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+    } else if (lane == 0 && rank == 0) {
       // --------------------------------------------------------- MMA issuer
       int it = 0, j = 0;
       bool ok = true;
@@ -237,6 +328,100 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
       tc::commit<CG>(dev::smem_addr(&mma_done));
       if (!dev::mbar_wait_bounded(dev::smem_addr(&mma_done), 0))
         dev::report_status(status, CMB_ERR_TIMEOUT);
+    }
+  } else if constexpr (Cfg::kHeld) {
+    // ---------------------------------------------------- held epilogue
+    // Warp w reads TMEM lane quarter w % 4; the two warps of a quarter take
+    // 128 columns each of one N=256 half.  Per half: four 32-column TMEM
+    // loads into registers, hand the half back to the MMA issuer, then write
+    // four 32 x 32 boxes (TMA store through the warp's staging box, or
+    // streaming stores).
+    const int q = warp & 3;
+    const int ew = warp - 2;
+    const int h = ew >> 2;
+    float scale = 1.0f;
+    if constexpr (kFp8) scale = __ldg(scale_a) * __ldg(scale_b);
+    const bool vec_ok = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    uint8_t *box = ring + (size_t)Cfg::kStages * Cfg::kStageBytes + (size_t)ew * Cfg::kEpiBoxBytes;
+    uint32_t epi_count = 0;
+    int j = 0;
+    for (int t = cluster; t < tiles; t += nclusters, ++j) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&tfull[0]), static_cast<uint32_t>(j) & 1) ||
+          *(volatile int *)&abort_flag) {
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+        atomicExch(&abort_flag, 1);
+        break;
+      }
+      tc::fence_after_sync();
+      const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta + q * 32;
+      const int row = row0 + lane;
+      float *crow = C + (size_t)row * N;
+#pragma unroll 1
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                               static_cast<uint32_t>(u * Cfg::kBn + h * 128);
+        uint32_t r[4][32];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tc::ld_32x32b_x32(taddr + 32 * i, r[i]);
+        tc::wait_ld();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t eb = dev::smem_addr(&tempty[u]);
+          if constexpr (CG == 1) dev::mbar_arrive(eb);
+          else dev::mbar_arrive_cluster(tc::map_to_cta(eb, 0));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int col0 = tn * Cfg::kTileN + u * Cfg::kBn + h * 128 + 32 * i;
+          if constexpr (kTmaEpi) {
+            // Same 128-byte-swizzled staging as the two-box epilogue; the
+            // one box is rewritten only after the store that last read it.
+            if (row0 < M && col0 < N) {  // warp-uniform
+              if (epi_count != 0) {
+                if (lane == 0) dev::bulk_wait_group_read<0>();
+                __syncwarp();
+              }
+              const uint32_t rb = dev::smem_addr(box) + lane * 128;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const uint32_t addr = rb + ((static_cast<uint32_t>(c) ^ (lane & 7)) << 4);
+                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
+                             "f"(scale * __uint_as_float(r[i][4 * c])),
+                             "f"(scale * __uint_as_float(r[i][4 * c + 1])),
+                             "f"(scale * __uint_as_float(r[i][4 * c + 2])),
+                             "f"(scale * __uint_as_float(r[i][4 * c + 3]))
+                             : "memory");
+              }
+              dev::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
+                dev::bulk_commit_group();
+              }
+              ++epi_count;
+            }
+          } else if (row < M) {
+            if (vec_ok && col0 + 32 <= N) {
+#pragma unroll
+              for (int c = 0; c < 32; c += 4)
+                st_cs_f4(crow + col0 + c, scale * __uint_as_float(r[i][c]),
+                         scale * __uint_as_float(r[i][c + 1]), scale * __uint_as_float(r[i][c + 2]),
+                         scale * __uint_as_float(r[i][c + 3]));
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (col0 + c < N) crow[col0 + c] = scale * __uint_as_float(r[i][c]);
+            }
+          }
+        }
+      }
+    }
+    if constexpr (kTmaEpi) {
+      if (lane == 0) dev::bulk_wait_group<0>();  // stores complete before the CTA leaves
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -436,10 +621,12 @@ int gemm_checks(const char *fn, const void *A, const void *B, const float *C, in
 }
 
 // Default shapes (from sweeps on B200 against cuBLAS measured alongside):
-// 1-CTA 128x256 tiles with 4 stages of 48 KiB; 2-CTA 256x512 tiles with 4
-// stages of 48 KiB per CTA; raster groups of 8 tile rows; 4 epilogue warps;
-// the TMA-store epilogue whenever C's row pitch allows a tensor map
-// (N % 4 == 0, 16-byte aligned C).
+// 1-CTA 128x256 tiles with 4 stages of 48 KiB and 4 epilogue warps; 2-CTA
+// 256x512 tiles with 4 stages of 48 KiB per CTA and the 8-warp held
+// epilogue (1-3 % over 4 warps: the MMAs of the next tile restart after
+// half of the drain); raster groups of 8 tile rows; the TMA-store epilogue
+// whenever C's row pitch allows a tensor map (N % 4 == 0, 16-byte aligned
+// C).
 template <bool kFp8, bool kTmaEpi>
 int dispatch_stages(const void *A, const void *B, float *C, int M, int N, int K,
                     const float *scale_a, const float *scale_b, int cta_group, int stages,
@@ -450,7 +637,7 @@ int dispatch_stages(const void *A, const void *B, float *C, int M, int N, int K,
                                                       group_m, status, stream);
   if (tile_n == 0) tile_n = cta_group == 2 ? 512 : 256;
   if (stages == 0) stages = 4;
-  if (epi_warps == 0) epi_warps = 4;
+  if (epi_warps == 0) epi_warps = tile_n == 512 ? 8 : 4;
   CMB_GEMM_CASE(1, 3, 1, 4)
   CMB_GEMM_CASE(1, 4, 1, 4)
   CMB_GEMM_CASE(2, 4, 1, 4)
@@ -459,9 +646,9 @@ int dispatch_stages(const void *A, const void *B, float *C, int M, int N, int K,
   CMB_GEMM_CASE(2, 3, 2, 4)
   CMB_GEMM_CASE(2, 4, 2, 4)
   CMB_GEMM_CASE(2, 3, 2, 8)
+  CMB_GEMM_CASE(2, 4, 2, 8)
   if constexpr (!kTmaEpi) {
     CMB_GEMM_CASE(2, 7, 1, 4)
-    CMB_GEMM_CASE(2, 4, 2, 8)
   }
 #undef CMB_GEMM_CASE
   return fail(CMB_ERR_INVALID_ARG,

@@ -210,8 +210,10 @@ int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int N, int K,
  * N % 4 == 0), 0 = default (2 when possible); tile_n = output columns per
  * tile, 256 or (cta_group 2, stages 3-4) 512 = two N=256 MMAs per K slice
  * into all 512 TMEM columns, 0 = default (512 for cta_group 2, else 256);
- * epi_warps = epilogue warps, 4 or (tile_n 512, stages 3, or stages 4 with
- * epilogue 1) 8, 0 = default (4). */
+ * epi_warps = epilogue warps, 4 or (tile_n 512, stages 3-4) 8 = each warp
+ * drains 128 columns of one N=256 half through registers and the half is
+ * handed back to the next tile's MMAs before it is stored, 0 = default
+ * (8 for tile_n 512, else 4). */
 int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int N, int K, int fp8,
                    const float *scale_a, const float *scale_b, int cta_group, int stages,
                    int group_m, int epilogue, int tile_n, int epi_warps, int *status,

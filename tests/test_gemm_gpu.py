@@ -129,7 +129,7 @@ def test_gemm_e4m3(cuda, cmb, orc, cg, M, N, K):
 @pytest.mark.parametrize("cg,stages,epi,tile_n,ew", [
     (1, 3, 1, 256, 4), (1, 4, 2, 256, 4), (2, 4, 1, 256, 4), (2, 5, 2, 256, 4), (2, 6, 2, 256, 4),
     (2, 7, 1, 256, 4), (2, 3, 2, 512, 4), (2, 4, 2, 512, 4), (2, 4, 1, 512, 4), (2, 3, 2, 512, 8),
-    (2, 4, 1, 512, 8)])
+    (2, 4, 1, 512, 8), (2, 4, 2, 512, 8)])
 def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi, tile_n, ew):
     M, N, K = 700, 520, 1040
     A = _normal_bf16(cuda, cmb, M, K, 31, K ** -0.5)
@@ -152,6 +152,41 @@ def test_gemm_tuned_shapes(cuda, cmb, orc, fp8, cg, stages, epi, tile_n, ew):
     assert int(status.item()) == 0
     _check_tiles(orc, a_h, b_h, C.cpu().numpy().reshape(M, N), K, [(0, 0, M, N)], dtype=dt,
                  sa=s_a, sb=s_b)
+
+
+@pytest.mark.parametrize("fp8", [0, 1])
+@pytest.mark.parametrize("epi", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 64), (4096, 4600, 208), (6144, 8192, 1024)])
+def test_gemm_held_epilogue_many_tiles(cuda, cmb, orc, fp8, epi, M, N, K):
+    """256 x 512 tiles with 8 epilogue warps: each half of the accumulator
+    is handed back before it is stored, and the next tile's MMAs start on
+    half 0 over the stages already loaded.  Sizes give most clusters two or
+    more tiles, K shorter than the ring (one K block) and a ragged last K
+    block and column edge."""
+    A = _normal_bf16(cuda, cmb, M, K, 51, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 52, K ** -0.5)
+    C = cuda.full((M * N,), float("nan"), dtype=cuda.float32, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    if fp8:
+        qa, sa = _quantize(cuda, cmb, A)
+        qb, sb = _quantize(cuda, cmb, B)
+        args = (dptr(qa), dptr(qb), dptr(C), M, N, K, 1, dptr(sa), dptr(sb))
+        a_h, b_h, dt = qa.cpu().numpy(), qb.cpu().numpy(), 1
+        s_a, s_b = float(sa[0].item()), float(sb[0].item())
+    else:
+        args = (dptr(A), dptr(B), dptr(C), M, N, K, 0, None, None)
+        a_h, b_h, dt = A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16), 0
+        s_a = s_b = 1.0
+    cmb.check("cmb_gemm_tuned", *args, 2, 4, 8, epi, 512, 8, dptr(status), stream_handle(cuda))
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    out = C.cpu().numpy().reshape(M, N)
+    assert not np.isnan(out).any()
+    rng = np.random.default_rng(M + N + K)
+    tiles = [(int(r) * 64, int(c) * 64, 64, 64)
+             for r, c in zip(rng.integers(0, M // 64, 48), rng.integers(0, N // 64, 48))]
+    tiles.append((M - 64, N - 64, 64, 64))  # the last tile's corner, ragged columns included
+    _check_tiles(orc, a_h, b_h, out, K, tiles, dtype=dt, sa=s_a, sb=s_b)
 
 
 @pytest.mark.parametrize("cg", [1, 2])
