@@ -556,8 +556,8 @@ def probe_gemm(torch, stream, sh, peaks):
 
 def probe_p2p(args, ranks) -> dict:
     """Config: 256 MiB seeded random bytes per GPU exchanged over NVLink,
-    ring (-> rank+1) and all-to-all (N chunks), by in-kernel peer stores and
-    by the copy engines; bit-exact receive check.  Time = max over ranks of
+    ring (-> rank+1) and all-to-all (N chunks), by in-kernel peer stores, by
+    in-kernel bulk copies and by the copy engines; bit-exact receive check.  Time = max over ranks of
     each rank's device time (CUDA events), median of 5 repetitions."""
     import torch
 
@@ -571,7 +571,7 @@ def probe_p2p(args, ranks) -> dict:
     try:
         for mode in ("ring", "alltoall"):
             egress = multi_gpu.egress_bytes(mode, ranks.rank, ranks.world, nbytes)
-            for method in ("store", "copy_engine"):
+            for method in ("store", "bulk", "copy_engine"):
                 times = []
                 for rep in range(2 + 5):
                     a = torch.cuda.Event(enable_timing=True)
@@ -595,6 +595,8 @@ def probe_p2p(args, ranks) -> dict:
                     "frac_of_900_spec": round(link / 900.0, 4),
                     "frac_of_770_measured_peer_copy": round(link / 770.0, 4),
                     "ms": round(ms, 4), "egress_bytes_per_gpu": egress,
+                    "sm_ctas": {"store": "2 per SM", "bulk": "32 in all",
+                                "copy_engine": "0 (copy engines)"}[method],
                     "bit_exact": bad == 0}
     finally:
         ex.close()

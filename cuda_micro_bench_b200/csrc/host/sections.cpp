@@ -650,13 +650,14 @@ namespace {
 struct GpuSide {
   int dev = 0;
   void *send = nullptr, *recv = nullptr, *scratch = nullptr, *count = nullptr;
+  int *count_status = nullptr;  // status word of the bulk-copy kernel
   cudaEvent_t a = nullptr, b = nullptr;
 };
 
 int free_sides(std::vector<GpuSide> &g) {
   for (auto &s : g) {
     cudaSetDevice(s.dev);
-    for (void *p : {s.send, s.recv, s.scratch, s.count})
+    for (void *p : {s.send, s.recv, s.scratch, s.count, static_cast<void *>(s.count_status)})
       if (p) cudaFree(p);
     if (s.a) cudaEventDestroy(s.a);
     if (s.b) cudaEventDestroy(s.b);
@@ -665,7 +666,16 @@ int free_sides(std::vector<GpuSide> &g) {
 }
 
 // Launches one exchange step on every GPU; returns the max device time.
-int p2p_step(std::vector<GpuSide> &g, size_t bytes, bool alltoall, bool store, double *ms_out) {
+// How a P2P step moves bytes: in-kernel peer stores, in-kernel bulk copies,
+// or the copy engines.
+enum class P2PMethod { kStore, kBulk, kCopyEngine };
+
+const char *p2p_method_name(P2PMethod m) {
+  return m == P2PMethod::kStore ? "store" : m == P2PMethod::kBulk ? "bulk" : "copy_engine";
+}
+
+int p2p_step(std::vector<GpuSide> &g, size_t bytes, bool alltoall, P2PMethod method,
+             double *ms_out) {
   const int n = static_cast<int>(g.size());
   for (auto &s : g) {
     CMB_CUDA_TRY(cudaSetDevice(s.dev));
@@ -688,8 +698,10 @@ int p2p_step(std::vector<GpuSide> &g, size_t bytes, bool alltoall, bool store, d
       jobs = n;
     }
     CMB_CUDA_TRY(cudaEventRecord(s.a, nullptr));
-    TRY(store ? cmb_p2p_scatter_store(dst, src, nb, jobs, 0, nullptr)
-              : cmb_p2p_scatter_copy_engine(dst, src, nb, jobs, nullptr));
+    if (method == P2PMethod::kStore) TRY(cmb_p2p_scatter_store(dst, src, nb, jobs, 0, nullptr));
+    else if (method == P2PMethod::kBulk)
+      TRY(cmb_p2p_scatter_bulk(dst, src, nb, jobs, 0, s.count_status, nullptr));
+    else TRY(cmb_p2p_scatter_copy_engine(dst, src, nb, jobs, nullptr));
     CMB_CUDA_TRY(cudaEventRecord(s.b, nullptr));
   }
   double worst = 0;
@@ -737,6 +749,7 @@ int multi_gpu_body(std::vector<GpuSide> &g, size_t bytes) {
     CMB_CUDA_TRY(cudaMalloc(&s.recv, bytes));
     CMB_CUDA_TRY(cudaMalloc(&s.scratch, bytes));
     CMB_CUDA_TRY(cudaMalloc(&s.count, sizeof(unsigned long long)));
+    CMB_CUDA_TRY(cudaMalloc(&s.count_status, sizeof(int)));
     CMB_CUDA_TRY(cudaEventCreate(&s.a));
     CMB_CUDA_TRY(cudaEventCreate(&s.b));
     TRY(cmb_fill_bytes(static_cast<uint8_t *>(s.send), bytes, seed + s.dev, nullptr));
@@ -746,12 +759,24 @@ int multi_gpu_body(std::vector<GpuSide> &g, size_t bytes) {
     CMB_CUDA_TRY(cudaDeviceSynchronize());
   }
   for (int alltoall = 0; alltoall < 2; ++alltoall) {
-    for (int store = 1; store >= 0; --store) {
+    for (P2PMethod method : {P2PMethod::kStore, P2PMethod::kBulk, P2PMethod::kCopyEngine}) {
       std::vector<double> ms;
+      for (auto &s : g) {
+        CMB_CUDA_TRY(cudaSetDevice(s.dev));
+        CMB_CUDA_TRY(cudaMemset(s.count_status, 0, sizeof(int)));
+      }
       for (int r = 0; r < 6; ++r) {
         double t = 0;
-        TRY(p2p_step(g, bytes, alltoall != 0, store != 0, &t));
+        TRY(p2p_step(g, bytes, alltoall != 0, method, &t));
         if (r > 0) ms.push_back(t);
+      }
+      for (auto &s : g) {
+        CMB_CUDA_TRY(cudaSetDevice(s.dev));
+        int st = 0;
+        CMB_CUDA_TRY(cudaMemcpy(&st, s.count_status, sizeof(int), cudaMemcpyDeviceToHost));
+        if (st != 0)
+          return fail(st, "p2p %s on device %d: kernel status %d (%s)", p2p_method_name(method),
+                      s.dev, st, cmb_status_string(st));
       }
       std::sort(ms.begin(), ms.end());
       const double t = ms[ms.size() / 2];
@@ -760,7 +785,7 @@ int multi_gpu_body(std::vector<GpuSide> &g, size_t bytes) {
       if (!ok) return fail(CMB_ERR_MISMATCH, "p2p %s: received bytes differ", alltoall ? "all-to-all" : "ring");
       const double egress = alltoall ? (double)bytes * (n - 1) / n : (double)bytes;
       const double link = gb_per_s(egress, t);
-      const std::string k = std::string(alltoall ? "alltoall_" : "ring_") + (store ? "store" : "copy_engine");
+      const std::string k = std::string(alltoall ? "alltoall_" : "ring_") + p2p_method_name(method);
       printf("  %-22s %d GPUs: %.1f GB/s egress per GPU (%.1f%% of 900), %.1f GB/s aggregate, bit-exact\n",
              k.c_str(), n, link, 100 * link / 900.0, n * link);
       g_results.log("p2p", k + "_link_gbps", link, "GB/s");

@@ -1,16 +1,20 @@
 // p2p.cu — multi-GPU probe: NVLink peer copies (new; the reference only asks
 // cudaDeviceCanAccessPeer, src/pcie.cu:100-112).
 //
-// Two ways to move bytes to another GPU over NVLink / NVSwitch:
+// Three ways to move bytes to another GPU over NVLink / NVSwitch:
 //   - in-kernel peer stores: SMs of the sending GPU load their own HBM with
-//     wide vector loads and issue 16-byte stores to a pointer that maps the
-//     receiver's memory (cudaIpcOpenMemHandle in multi-process use,
+//     wide vector loads and issue 16- or 32-byte stores to a pointer that
+//     maps the receiver's memory (cudaIpcOpenMemHandle in multi-process use,
 //     cudaDeviceEnablePeerAccess in one process);
+//   - in-kernel bulk copies: one thread per CTA streams chunks of its own
+//     HBM into a shared-memory ring with cp.async.bulk loads (this GPU's
+//     memory only, one destination CTA) and writes each chunk to the peer
+//     pointer with one cp.async.bulk store;
 //   - the copy engines: cudaMemcpyAsync between the two devices' pointers.
 // A "job" is one (src, dst, bytes) copy; a scatter runs up to 8 jobs at once
 // (one per destination GPU), which covers the ring (one job) and the
-// all-to-all (one job per peer).  No TMA and no collective library is used,
-// and no kernel waits on another GPU: completion is observed on the host.
+// all-to-all (one job per peer).  No collective library is used, and no
+// kernel waits on another GPU: completion is observed on the host.
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -23,6 +27,7 @@ namespace {
 
 constexpr int kMaxJobs = 8;
 constexpr int kP2PThreads = 256;
+constexpr int kBulkCtas = 32;  // default CTAs of a bulk scatter, over all jobs
 
 struct Jobs {
   const char *src[kMaxJobs];
@@ -94,6 +99,59 @@ __global__ void __launch_bounds__(kP2PThreads) k_p2p_store(Jobs jobs) {
   }
   if (blockIdx.x == 0)
     for (size_t i = nvec * VB + threadIdx.x; i < bytes; i += kP2PThreads) dst[i] = src[i];
+}
+
+// Bulk-copy form: blockIdx.y = job; CTA x takes chunks x, x + gridDim.x, ...
+// of the job's 16-byte-aligned body.  One thread keeps S - G + 1 chunk loads
+// and G chunk stores in flight over an S-stage ring: after the store of
+// chunk i it waits until at most G - 1 stores still read shared memory, then
+// reloads the stage of chunk i + 1 - G with chunk i + 1 - G + S.  The body's
+// last (< 16) bytes are copied by plain stores in CTA 0.
+template <int S, int G>
+__global__ void __launch_bounds__(32) k_p2p_bulk(Jobs jobs, uint32_t chunk, int *status) {
+  static_assert(G >= 1 && 2 * G <= S, "stores in flight must leave loads in flight");
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ __align__(8) uint64_t full[S];
+  const int j = blockIdx.y;
+  const char *__restrict__ src = jobs.src[j];
+  char *__restrict__ dst = jobs.dst[j];
+  const size_t bytes = jobs.bytes[j];
+  const size_t body = bytes & ~static_cast<size_t>(15);
+  const size_t nchunks = (body + chunk - 1) / chunk;
+  const size_t mine =
+      nchunks > blockIdx.x ? (nchunks - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  if (threadIdx.x == 0 && mine > 0) {
+    for (int s = 0; s < S; ++s) dev::mbar_init(dev::smem_addr(&full[s]), 1);
+    dev::fence_mbar_init();
+    const auto off = [&](size_t i) { return (blockIdx.x + i * gridDim.x) * (size_t)chunk; };
+    const auto len = [&](size_t i) {
+      const size_t o = off(i);
+      return static_cast<uint32_t>(body - o < chunk ? body - o : chunk);
+    };
+    const auto load = [&](size_t i) {
+      const int s = static_cast<int>(i % S);
+      const uint32_t bar = dev::smem_addr(&full[s]);
+      dev::mbar_arrive_expect_tx(bar, len(i));
+      dev::bulk_load(dev::smem_addr(ring + (size_t)s * chunk), src + off(i), len(i), bar);
+    };
+    for (size_t i = 0; i < mine && i < (size_t)S; ++i) load(i);
+    for (size_t i = 0; i < mine; ++i) {
+      const int s = static_cast<int>(i % S);
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), static_cast<uint32_t>(i / S) & 1)) {
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+        break;
+      }
+      dev::bulk_store(dst + off(i), dev::smem_addr(ring + (size_t)s * chunk), len(i));
+      dev::bulk_commit_group();
+      if (i + 1 >= (size_t)G && i + 1 - G + S < mine) {
+        dev::bulk_wait_group_read<G - 1>();
+        load(i + 1 - G + S);
+      }
+    }
+    dev::bulk_wait_group<0>();  // every store has written its bytes
+  }
+  if (blockIdx.x == 0)
+    for (size_t i = body + threadIdx.x; i < bytes; i += 32) dst[i] = src[i];
 }
 
 struct CeStreams {
@@ -239,6 +297,73 @@ extern "C" int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *
                                            const size_t *bytes, int n, int ctas_per_job,
                                            int vec_bytes, cmb_stream_t stream) {
   return scatter_store(dst, src, bytes, n, ctas_per_job, vec_bytes, stream);
+}
+
+namespace cmb {
+namespace {
+
+template <int S, int G>
+int launch_bulk(const Jobs &jobs, int n, int ctas_per_job, uint32_t chunk, int *status,
+                cudaStream_t stream) {
+  const size_t smem = (size_t)S * chunk;
+  auto kern = k_p2p_bulk<S, G>;
+  CMB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  kern<<<dim3(ctas_per_job, n), 32, smem, stream>>>(jobs, chunk, status);
+  CMB_LAUNCH_CHECK();
+  return CMB_OK;
+}
+
+int scatter_bulk(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                 int ctas_per_job, int chunk_bytes, int stages, int *status, cudaStream_t stream) {
+  const char *fn = "cmb_p2p_scatter_bulk";
+  int rc = check_jobs(fn, dst, src, bytes, n);
+  if (rc) return rc;
+  if (chunk_bytes == 0) chunk_bytes = 16 << 10;
+  if (stages == 0) stages = 8;
+  if (chunk_bytes < 16 || chunk_bytes % 16 != 0 || chunk_bytes > (64 << 10))
+    return fail(CMB_ERR_INVALID_ARG, "%s: chunk_bytes %d not a multiple of 16 in [16, 65536]", fn,
+                chunk_bytes);
+  if (stages != 4 && stages != 8)
+    return fail(CMB_ERR_INVALID_ARG, "%s: stages %d not 4 or 8", fn, stages);
+  if ((size_t)stages * chunk_bytes > (size_t)(227 << 10))
+    return fail(CMB_ERR_INVALID_ARG, "%s: %d stages x %d bytes exceed 227 KiB of shared memory",
+                fn, stages, chunk_bytes);
+  Jobs jobs = {};
+  size_t most = 0;
+  for (int j = 0; j < n; ++j) {
+    if ((reinterpret_cast<uintptr_t>(dst[j]) | reinterpret_cast<uintptr_t>(src[j])) & 15)
+      return fail(CMB_ERR_INVALID_ARG, "%s: job %d not 16-byte aligned", fn, j);
+    jobs.src[j] = static_cast<const char *>(src[j]);
+    jobs.dst[j] = static_cast<char *>(dst[j]);
+    jobs.bytes[j] = bytes[j];
+    most = bytes[j] > most ? bytes[j] : most;
+  }
+  if (most == 0) return CMB_OK;
+  // 32 CTAs in all reach the SM-side write ceiling (~680 GB/s per GPU on
+  // B200 NVLink 5, the same as peer stores from every SM); the rest of the
+  // GPU stays free.
+  if (ctas_per_job <= 0) ctas_per_job = (kBulkCtas + n - 1) / n < 4 ? 4 : (kBulkCtas + n - 1) / n;
+  const size_t want = (most + chunk_bytes - 1) / chunk_bytes;
+  if ((size_t)ctas_per_job > want) ctas_per_job = static_cast<int>(want == 0 ? 1 : want);
+  const uint32_t c = static_cast<uint32_t>(chunk_bytes);
+  return stages == 4 ? launch_bulk<4, 2>(jobs, n, ctas_per_job, c, status, stream)
+                     : launch_bulk<8, 4>(jobs, n, ctas_per_job, c, status, stream);
+}
+
+}  // namespace
+}  // namespace cmb
+
+extern "C" int cmb_p2p_scatter_bulk(void *const *dst, const void *const *src, const size_t *bytes,
+                                    int n, int ctas_per_job, int *status, cmb_stream_t stream) {
+  return scatter_bulk(dst, src, bytes, n, ctas_per_job, 0, 0, status, stream);
+}
+
+extern "C" int cmb_p2p_scatter_bulk_tuned(void *const *dst, const void *const *src,
+                                          const size_t *bytes, int n, int ctas_per_job,
+                                          int chunk_bytes, int stages, int *status,
+                                          cmb_stream_t stream) {
+  return scatter_bulk(dst, src, bytes, n, ctas_per_job, chunk_bytes, stages, status, stream);
 }
 
 extern "C" int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src,

@@ -114,6 +114,8 @@ class PeerExchange:
         nb = (ctypes.c_size_t * n)(*[j.nbytes for j in jobs])
         if method == "store":
             self.capi.check("cmb_p2p_scatter_store", dst, src, nb, n, 0, stream)
+        elif method == "bulk":
+            self.capi.check("cmb_p2p_scatter_bulk", dst, src, nb, n, 0, None, stream)
         elif method == "copy_engine":
             self.capi.check("cmb_p2p_scatter_copy_engine", dst, src, nb, n, stream)
         else:

@@ -286,6 +286,22 @@ int cmb_p2p_scatter_store(void *const *dst, const void *const *src, const size_t
  * every job is 32-byte aligned. */
 int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *src, const size_t *bytes,
                                 int n, int ctas_per_job, int vec_bytes, cmb_stream_t stream);
+/* The same n copies by cp.async.bulk: one thread per CTA streams 16 KiB
+ * chunks of src (this GPU's memory) through an 8-stage shared-memory ring
+ * and writes each chunk to dst (which may be a peer's memory) with one bulk
+ * store.  16-byte aligned pointers; ctas_per_job <= 0 picks 32 CTAs in all
+ * (at least 4 per job), which reach the same NVLink rate as peer stores
+ * from every SM; *status (device, may be NULL) = CMB_ERR_TIMEOUT if a chunk
+ * load never completed within 2 s.  No reference counterpart (new NVLink
+ * probe). */
+int cmb_p2p_scatter_bulk(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                         int ctas_per_job, int *status, cmb_stream_t stream);
+/* cmb_p2p_scatter_bulk with an explicit chunk size (multiple of 16, at most
+ * 64 KiB, 0 = 16 KiB) and ring depth (4 stages with 2 stores in flight, or 8
+ * with 4; 0 = 8; stages x chunk <= 227 KiB), for sweeps. */
+int cmb_p2p_scatter_bulk_tuned(void *const *dst, const void *const *src, const size_t *bytes,
+                               int n, int ctas_per_job, int chunk_bytes, int stages, int *status,
+                               cmb_stream_t stream);
 /* The same n copies by the copy engines (cudaMemcpyAsync, one internal
  * stream per job, joined back into `stream`). */
 int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src, const size_t *bytes,

@@ -18,23 +18,66 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 EXE = os.path.join(ROOT, "cuda_micro_bench_b200", "bin", "cmb_b200")
 
 
-@pytest.mark.parametrize("method", ["store", "copy_engine"])
-@pytest.mark.parametrize("sizes", [[1 << 20], [4096 + 48, 7 << 16, 16], [5 << 20] * 8])
-def test_scatter_local_bit_exact(cuda, cmb, method, sizes):
-    n = len(sizes)
+def _local_jobs(cuda, sizes):
     src = [cuda.randint(0, 255, (s,), dtype=cuda.uint8, device="cuda") for s in sizes]
     dst = [cuda.zeros(s + 64, dtype=cuda.uint8, device="cuda") for s in sizes]
+    n = len(sizes)
     d = (ctypes.c_void_p * n)(*[t.data_ptr() for t in dst])
     s_ = (ctypes.c_void_p * n)(*[t.data_ptr() for t in src])
     nb = (ctypes.c_size_t * n)(*sizes)
-    if method == "store":
-        cmb.check("cmb_p2p_scatter_store", d, s_, nb, n, 0, stream_handle(cuda))
-    else:
-        cmb.check("cmb_p2p_scatter_copy_engine", d, s_, nb, n, stream_handle(cuda))
-    cuda.cuda.synchronize()
+    return src, dst, d, s_, nb
+
+
+def _check_jobs(cuda, src, dst, sizes):
     for a, b, sz in zip(src, dst, sizes):
         assert cuda.equal(a, b[:sz])
         assert int(b[sz:].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("method", ["store", "bulk", "copy_engine"])
+@pytest.mark.parametrize("sizes", [[1 << 20], [4096 + 48, 7 << 16, 16], [5 << 20] * 8,
+                                   [(32 << 10) * 149 + 13, 0, 15, 1 << 16]])
+def test_scatter_local_bit_exact(cuda, cmb, method, sizes):
+    n = len(sizes)
+    src, dst, d, s_, nb = _local_jobs(cuda, sizes)
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    if method == "store":
+        cmb.check("cmb_p2p_scatter_store", d, s_, nb, n, 0, stream_handle(cuda))
+    elif method == "bulk":
+        cmb.check("cmb_p2p_scatter_bulk", d, s_, nb, n, 0, dptr(status), stream_handle(cuda))
+    else:
+        cmb.check("cmb_p2p_scatter_copy_engine", d, s_, nb, n, stream_handle(cuda))
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    _check_jobs(cuda, src, dst, sizes)
+
+
+@pytest.mark.parametrize("chunk,stages,ctas", [(16, 4, 3), (4096, 8, 0), (56 << 10, 4, 1),
+                                               (16 << 10, 8, 200), (32 << 10, 4, 0)])
+def test_scatter_bulk_shapes(cuda, cmb, chunk, stages, ctas):
+    """Ring depths, chunk sizes from one 16-byte line to 64 KiB, more CTAs
+    than chunks, one CTA walking every chunk, ragged tails."""
+    sizes = [(3 << 20) + 16 * 7 + 5, 4096, 17, (1 << 20) + 32]
+    n = len(sizes)
+    src, dst, d, s_, nb = _local_jobs(cuda, sizes)
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    cmb.check("cmb_p2p_scatter_bulk_tuned", d, s_, nb, n, ctas, chunk, stages, dptr(status),
+              stream_handle(cuda))
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    _check_jobs(cuda, src, dst, sizes)
+
+
+def test_scatter_bulk_rejects_bad_args(cuda, cmb):
+    t = cuda.zeros(1 << 16, dtype=cuda.uint8, device="cuda")
+    one = lambda off: (ctypes.c_void_p * 1)(t.data_ptr() + off)
+    nb = (ctypes.c_size_t * 1)(4096)
+    s = stream_handle(cuda)
+    assert cmb.lib.cmb_p2p_scatter_bulk(one(8), one(0), nb, 1, 0, None, s) == 1  # alignment
+    assert cmb.lib.cmb_p2p_scatter_bulk_tuned(one(0), one(4096), nb, 1, 0, 24, 4, None, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_bulk_tuned(one(0), one(4096), nb, 1, 0, 4096, 6, None, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_bulk_tuned(one(0), one(4096), nb, 1, 0, 65536, 8, None, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_bulk(one(0), one(4096), nb, 9, 0, None, s) == 1  # > 8 jobs
 
 
 def test_cli_p2p_section(cuda, tmp_path):
@@ -45,7 +88,8 @@ def test_cli_p2p_section(cuda, tmp_path):
     count = cuda.cuda.device_count()
     assert res["pcie"]["device_count"]["value"] == count
     if count >= 2:
-        for k in ("ring_store", "ring_copy_engine", "alltoall_store", "alltoall_copy_engine"):
+        for k in ("ring_store", "ring_bulk", "ring_copy_engine", "alltoall_store",
+                  "alltoall_bulk", "alltoall_copy_engine"):
             assert res["p2p"][k + "_verified"]["value"] == 1.0
             assert res["p2p"][k + "_link_gbps"]["value"] > 10.0
 
@@ -72,7 +116,7 @@ def _rank(rank, world, port, q):
     bad = {}
     sh = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for mode in ("ring", "alltoall"):
-        for method in ("store", "copy_engine"):
+        for method in ("store", "bulk", "copy_engine"):
             ranks.barrier()
             ex.launch(mode, method, sh)
             torch.cuda.synchronize()
