@@ -595,7 +595,7 @@ def probe_p2p(args, ranks) -> dict:
                     "frac_of_900_spec": round(link / 900.0, 4),
                     "frac_of_770_measured_peer_copy": round(link / 770.0, 4),
                     "ms": round(ms, 4), "egress_bytes_per_gpu": egress,
-                    "sm_ctas": {"store": "2 per SM", "bulk": "32 in all",
+                    "sm_ctas": {"store": "2 per SM", "bulk": "32 per job (<= SMs / jobs)",
                                 "copy_engine": "0 (copy engines)"}[method],
                     "bit_exact": bad == 0}
     finally:

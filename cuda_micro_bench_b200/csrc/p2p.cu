@@ -27,7 +27,7 @@ namespace {
 
 constexpr int kMaxJobs = 8;
 constexpr int kP2PThreads = 256;
-constexpr int kBulkCtas = 32;  // default CTAs of a bulk scatter, over all jobs
+constexpr int kBulkCtasPerJob = 32;  // default CTAs per job of a bulk scatter
 
 struct Jobs {
   const char *src[kMaxJobs];
@@ -340,10 +340,13 @@ int scatter_bulk(void *const *dst, const void *const *src, const size_t *bytes, 
     most = bytes[j] > most ? bytes[j] : most;
   }
   if (most == 0) return CMB_OK;
-  // 32 CTAs in all reach the SM-side write ceiling (~680 GB/s per GPU on
-  // B200 NVLink 5, the same as peer stores from every SM); the rest of the
-  // GPU stays free.
-  if (ctas_per_job <= 0) ctas_per_job = (kBulkCtas + n - 1) / n < 4 ? 4 : (kBulkCtas + n - 1) / n;
+  // 32 CTAs per job (at most one per SM in all): on a ring they reach the
+  // SM-side write ceiling (~680 GB/s per GPU on B200 NVLink 5, the same as
+  // peer stores from every SM) and leave the rest of the GPU free.
+  if (ctas_per_job <= 0) {
+    const int per_sm = current_sm_count() / n;
+    ctas_per_job = per_sm < kBulkCtasPerJob ? (per_sm < 1 ? 1 : per_sm) : kBulkCtasPerJob;
+  }
   const size_t want = (most + chunk_bytes - 1) / chunk_bytes;
   if ((size_t)ctas_per_job > want) ctas_per_job = static_cast<int>(want == 0 ? 1 : want);
   const uint32_t c = static_cast<uint32_t>(chunk_bytes);

@@ -289,9 +289,9 @@ int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *src, const 
 /* The same n copies by cp.async.bulk: one thread per CTA streams 16 KiB
  * chunks of src (this GPU's memory) through an 8-stage shared-memory ring
  * and writes each chunk to dst (which may be a peer's memory) with one bulk
- * store.  16-byte aligned pointers; ctas_per_job <= 0 picks 32 CTAs in all
- * (at least 4 per job), which reach the same NVLink rate as peer stores
- * from every SM; *status (device, may be NULL) = CMB_ERR_TIMEOUT if a chunk
+ * store.  16-byte aligned pointers; ctas_per_job <= 0 picks 32 (at most
+ * SMs / n), which on a ring reach the same NVLink rate as peer stores from
+ * every SM; *status (device, may be NULL) = CMB_ERR_TIMEOUT if a chunk
  * load never completed within 2 s.  No reference counterpart (new NVLink
  * probe). */
 int cmb_p2p_scatter_bulk(void *const *dst, const void *const *src, const size_t *bytes, int n,
