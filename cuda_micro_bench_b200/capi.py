@@ -73,6 +73,9 @@ SIGNATURES = {
     "cmb_benchmark_tensor_core_extended": (_i, []),
     "cmb_benchmark_multi_gpu": (_i, []),
     "cmb_results_log_report_placeholders": (_i, []),
+    "cmb_report_key_count": (ctypes.c_size_t, []),
+    "cmb_report_key": (_i, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_char_p),
+                            ctypes.POINTER(ctypes.c_char_p)]),
     "cmb_run_cli": (_i, [_i, _p, _s]),
     "cmb_results_set_device": (_i, [_s, _s, _i, _i, _i, _i]),
     "cmb_results_log": (_i, [_s, _s, _d, _s]),

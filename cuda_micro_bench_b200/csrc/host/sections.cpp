@@ -847,12 +847,25 @@ int benchmark_multi_gpu() {
   return rc;
 }
 
-void log_report_placeholders() {
-  static const char *const kKeys[][2] = {
+namespace {
+// The (section, key) paths the reference's results/report.html reads.
+const char *const kReportKeys[][2] = {
 #include "report_keys.inc"
-  };
-  for (const auto &k : kKeys)
+};
+}  // namespace
+
+void log_report_placeholders() {
+  for (const auto &k : kReportKeys)
     if (!g_results.has(k[0], k[1])) g_results.log(k[0], k[1], 0.0, "N/A");
+}
+
+size_t report_key_count() { return sizeof(kReportKeys) / sizeof(kReportKeys[0]); }
+
+bool report_key(size_t i, const char **section, const char **key) {
+  if (i >= report_key_count()) return false;
+  *section = kReportKeys[i][0];
+  *key = kReportKeys[i][1];
+  return true;
 }
 
 namespace {
@@ -955,6 +968,15 @@ extern "C" int cmb_benchmark_tensor_core_extended(void) { return benchmark_tenso
 extern "C" int cmb_benchmark_multi_gpu(void) { return benchmark_multi_gpu(); }
 extern "C" int cmb_results_log_report_placeholders(void) {
   log_report_placeholders();
+  return CMB_OK;
+}
+extern "C" size_t cmb_report_key_count(void) { return report_key_count(); }
+extern "C" int cmb_report_key(size_t i, const char **section, const char **key) {
+  if (section == nullptr || key == nullptr)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_report_key: null output pointer");
+  if (!report_key(i, section, key))
+    return fail(CMB_ERR_INVALID_ARG, "cmb_report_key: index %zu >= %zu keys", i,
+                report_key_count());
   return CMB_OK;
 }
 extern "C" int cmb_run_cli(int argc, const char *const *argv, const char *json_path) {

@@ -44,6 +44,9 @@ int benchmark_multi_gpu();           // --p2p         (new: sharded stream + NVL
 // Logs every results key the reference's report reads and no section
 // measured, as "N/A" (null), so the report renders.
 void log_report_placeholders();
+// The report's key table: its size, and entry i (false past the end).
+size_t report_key_count();
+bool report_key(size_t i, const char **section, const char **key);
 
 // The CLI (src/main.cu:156-181): flags run sections; no flags runs all and
 // writes `json_path`.  Returns the process exit code.

@@ -337,6 +337,11 @@ int cmb_benchmark_multi_gpu(void);           /* new: NVLink P2P and sharded stre
 /* Logs "N/A" for every key the reference's results/report.html reads that
  * no section logged, so the report renders. */
 int cmb_results_log_report_placeholders(void);
+/* The same key table, read-only: how many (section, key) paths the report
+ * reads, and path i as two static strings.  No reference counterpart (the
+ * reference keeps these paths only inside results/report.html). */
+size_t cmb_report_key_count(void);
+int cmb_report_key(size_t i, const char **section, const char **key);
 /* The CLI (src/main.cu:156-181) with results written to json_path (NULL:
  * results/results.json); returns the process exit code. */
 int cmb_run_cli(int argc, const char *const *argv, const char *json_path);

@@ -59,6 +59,8 @@ def test_cli_full_run(cuda, tmp_path):
     assert v("memory_more", "l2_aggregate_verified") == 1.0
     assert v("memory_more", "l2_aggregate_bw_gbps") > v("memory", "dram_read_bw_gbps")
     assert 5 < v("pcie", "htod_bandwidth_GiB_s") < 128 and 5 < v("pcie", "dtoh_bandwidth_GiB_s") < 128
+    from cuda_micro_bench_b200 import validate_results
+    assert validate_results.check(doc) == []
     print(p.stdout)
 
 
