@@ -44,7 +44,7 @@ MEASURED = [
     ("memory_dram", "copy_verified", 1.0, "bool"),
     ("memory_dram", "chase_endpoint_verified", 1.0, "bool"),
     ("memory_dram", "chase_working_set_bytes", 512.0 * 2**20, "bytes"),
-    ("memory_dram", "chase_loads_per_sample", 512.0 * 2**20 / 128, "loads"),
+    ("memory_dram", "chase_loads_per_sample", 4 * 512.0 * 2**20 / 128, "loads"),
     ("memory_dram", "chase_min_sector_footprint_bytes", 128.0 * 2**20, "bytes"),
     ("memory_dram", "stream_working_set_bytes", 2.0**30, "bytes"),
     ("memory_cache", "l2_chase_working_set_bytes", 64.0 * 2**20, "bytes"),
@@ -104,6 +104,7 @@ def _set(doc, sec, key, value, unit=None):
     ("memory", "dram_read_bw_gbps", 0.0, None, "HBM3e read"),
     ("memory_dram", "chase_working_set_bytes", 64.0 * 2**20, None, "fits in L2"),
     ("memory_dram", "chase_loads_per_sample", 1000.0, None, "128-byte slot"),
+    ("memory_dram", "chase_loads_per_sample", 1.5 * 512 * 2**20 / 128, None, "whole laps"),
     ("memory", "l2_latency_cyc", 20.0, None, "latency order"),
     ("memory_more", "l2_aggregate_bw_gbps", 6000.0, None, "not above the DRAM"),
     ("tma", "tile_copy_verified", 0.0, None, "output check failed"),
