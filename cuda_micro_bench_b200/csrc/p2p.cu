@@ -128,17 +128,25 @@ __global__ void __launch_bounds__(32) k_p2p_bulk(Jobs jobs, uint32_t chunk, int 
       const size_t o = off(i);
       return static_cast<uint32_t>(body - o < chunk ? body - o : chunk);
     };
+    size_t issued = 0;  // chunks whose load has been issued
     const auto load = [&](size_t i) {
       const int s = static_cast<int>(i % S);
       const uint32_t bar = dev::smem_addr(&full[s]);
       dev::mbar_arrive_expect_tx(bar, len(i));
       dev::bulk_load(dev::smem_addr(ring + (size_t)s * chunk), src + off(i), len(i), bar);
+      issued = i + 1;
     };
     for (size_t i = 0; i < mine && i < (size_t)S; ++i) load(i);
     for (size_t i = 0; i < mine; ++i) {
       const int s = static_cast<int>(i % S);
       if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), static_cast<uint32_t>(i / S) & 1)) {
         dev::report_status(status, CMB_ERR_TIMEOUT);
+        // wait (bounded) for the loads still writing the ring before the
+        // CTA's shared memory goes away
+        for (size_t k = i; k < issued; ++k)
+          if (!dev::mbar_wait_bounded(dev::smem_addr(&full[k % S]),
+                                      static_cast<uint32_t>(k / S) & 1, 100000000ull))
+            break;
         break;
       }
       dev::bulk_store(dst + off(i), dev::smem_addr(ring + (size_t)s * chunk), len(i));

@@ -82,6 +82,22 @@ def test_copy_full_size_1gib(cuda, cmb):
     assert cuda.equal(src.view(cuda.int32), dst.view(cuda.int32))
 
 
+def test_copy_headline_size_and_past_4gib(cuda, cmb):
+    """The bench's per-GPU workload (fp32[2^30], 4 GiB) and a copy whose
+    byte count passes 2^32 with a ragged tail: 64-bit offsets throughout."""
+    nbytes = (1 << 32) + 4096 + 36
+    src = cuda.empty(nbytes // 4 + 1, dtype=cuda.float32, device="cuda")
+    dst = cuda.zeros(nbytes // 4 + 2, dtype=cuda.float32, device="cuda")
+    cmb.check("cmb_fill_uniform_f32", dptr(src), src.numel(), ctypes.c_uint64(77),
+              stream_handle(cuda))
+    for n in (1 << 32, nbytes):
+        cmb.check("cmb_stream_copy", dptr(dst), dptr(src), n, stream_handle(cuda))
+        cuda.cuda.synchronize()
+        a, b = src.view(cuda.uint8)[:n], dst.view(cuda.uint8)[:n]
+        assert cuda.equal(a, b)
+    assert int(dst.view(cuda.uint8)[nbytes:].count_nonzero()) == 0
+
+
 def _sum(cuda, cmb, t, n=None, offset_elems=0):
     n = t.numel() - offset_elems if n is None else n
     ws_bytes = cmb.lib.cmb_stream_sum_workspace_bytes(n)
@@ -122,6 +138,17 @@ def test_sum_full_size_and_deterministic(cuda, cmb, orc):
     s1 = _sum(cuda, cmb, d, n=h)
     s2 = _sum(cuda, cmb, d, n=n - h, offset_elems=h)
     assert abs((s1 + s2) - ref) <= REL_TOL_SUM * abs(ref)
+
+
+def test_sum_past_4gib(cuda, cmb, orc):
+    """fp32[2^30 + 5]: the element count's byte size passes 2^32."""
+    n = (1 << 30) + 5
+    d = cuda.empty(n, dtype=cuda.float32, device="cuda")
+    cmb.check("cmb_fill_uniform_f32", dptr(d), n, ctypes.c_uint64(99), stream_handle(cuda))
+    got = _sum(cuda, cmb, d)
+    host = d.cpu().numpy()
+    ref = orc.orc_sum_f64(ptr(host), n, 0)
+    assert abs(got - ref) <= REL_TOL_SUM * max(abs(ref), 1.0), (got, ref)
 
 
 def test_sum_rejects_small_workspace(cuda, cmb):
