@@ -3,8 +3,8 @@
 One process per GPU (torchrun).  Every rank owns a send and a receive buffer
 of `nbytes` allocated with cmb_p2p_alloc; the ranks swap CUDA IPC handles of
 their receive buffers through torch.distributed, map the peers' buffers, and
-then write straight into them with the library's peer-store kernel or its
-copy-engine scatter.  torch.distributed carries only the handle exchange,
+then write straight into them with the library's peer-store kernel, its
+bulk-copy kernel or its copy-engine scatter.  torch.distributed carries only the handle exchange,
 barriers and the max-over-ranks timing reduction: the data path uses no
 collective library.
 
