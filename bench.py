@@ -62,8 +62,13 @@ class Ranks:
             import datetime
 
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            kw = {}
+            if backend == "nccl":
+                # bind the group to this rank's GPU (no guessing from the rank)
+                torch.cuda.set_device(self.local_rank)
+                kw["device_id"] = torch.device("cuda", self.local_rank)
             dist.init_process_group(backend=backend,
-                                    timeout=datetime.timedelta(seconds=timeout_s))
+                                    timeout=datetime.timedelta(seconds=timeout_s), **kw)
 
     def barrier(self):
         if self.world > 1:
