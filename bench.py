@@ -517,6 +517,18 @@ def probe_gemm(torch, stream, sh, peaks):
                       "frac_of_2250_spec": round(tf / 2250.0, 4), "ms": round(ms, 4),
                       "sampled_tiles_max_rel_err": err, "within_1e-2": err <= 1e-2,
                       "status": int(status.item())}
+    # the configuration's literal tile: 256 x 256 per 2-CTA pair (one N=256
+    # MMA per K slice, two accumulators so the epilogue overlaps)
+    fn = lambda: check("cmb_gemm_tuned", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
+                       ctypes.c_void_p(C.data_ptr()), M, N, K, 0, None, None, 2, 4, 8, 0, 256, 4,
+                       ctypes.c_void_p(status.data_ptr()), sh)
+    ms = _median_ms(torch, stream, fn)
+    tf = flop / (ms * 1e-3) / 1e12
+    err = sampled_err(a64, b64)
+    out["bf16_8192_2cta_256x256"] = {
+        "TFLOP/s": round(tf, 1), "frac_of_measured_bf16": round(tf / peaks["bf16_tflops"], 4),
+        "ms": round(ms, 4), "sampled_tiles_max_rel_err": err, "within_1e-2": err <= 1e-2,
+        "status": int(status.item())}
     del a64, b64
 
     def deq(q, s, rows_, cols_):
