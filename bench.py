@@ -633,7 +633,7 @@ def run_probe_only(args) -> int:
         if name == "stream":
             out.update(probe_stream_1gib(torch, stream, sh, peaks))
         elif name == "chase":
-            out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (24 if args.full_chase else 22))
+            out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (22 if args.quick_chase else 24))
         elif name == "tma":
             out["tma_16384"] = probe_tma(torch, stream, sh, peaks)
         elif name == "gemm":
@@ -696,7 +696,7 @@ def run_probes(args, ranks, peaks) -> dict:
         out["p2p_256mib"] = probe_p2p(args, ranks)
     if ranks.world == 1:
         out.update(probe_stream_1gib(torch, stream, sh, peaks))
-        out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (24 if args.full_chase else 22))
+        out["chase_512mib"] = probe_chase(torch, stream, sh, 1 << (22 if args.quick_chase else 24))
         torch.cuda.empty_cache()
         out["tma_16384"] = probe_tma(torch, stream, sh, peaks)
         torch.cuda.empty_cache()
@@ -745,7 +745,8 @@ def main(argv=None) -> int:
     ap.add_argument("--gib", type=float, default=4.0, help="copy size per GPU in GiB (default 4)")
     ap.add_argument("--no-probes", action="store_true", help="headline only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--full-chase", action="store_true", help="2^24 chase hops (default 2^22)")
+    ap.add_argument("--quick-chase", action="store_true",
+                    help="2^22 chase hops instead of the configuration's 2^24")
     ap.add_argument("--probe", action="append", choices=["stream", "chase", "tma", "gemm"],
                     help="run only this probe (repeatable); no headline line")
     args = ap.parse_args(argv)
