@@ -13,6 +13,8 @@
 #include <thread>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../../include/cmb_b200.h"
 #include "../cmb_host.h"
 #include "result_logger.h"
@@ -894,9 +896,18 @@ void usage(const char *name) {
   printf("  %-12s %s\n", "--all", "Run all sections (default)");
 }
 
+// Runs one section inside an NVTX range named by its flag, so a profiler's
+// timeline (or ncu --nvtx-include) can pick a section out of a full run.
+int run_section(const Section &s) {
+  nvtxRangePushA(s.flag + 2);  // "--memory" -> "memory"
+  const int rc = s.run();
+  nvtxRangePop();
+  return rc;
+}
+
 int run_all() {
   for (const auto &s : kSections) {
-    const int rc = s.run();
+    const int rc = run_section(s);
     if (rc != CMB_OK) return rc;
   }
   log_report_placeholders();
@@ -938,7 +949,7 @@ int run_cli(int argc, const char *const *argv, const char *json_path) {
       rc = run_all();
     } else {
       for (const auto &s : kSections)
-        if (std::strcmp(opt, s.flag) == 0) rc = s.run();
+        if (std::strcmp(opt, s.flag) == 0) rc = run_section(s);
     }
     if (rc == -1) {
       printf("Unknown option: %s\n", opt);
