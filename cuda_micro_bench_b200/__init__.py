@@ -6,6 +6,15 @@ CUDA for sm_100a behind the C ABI of ``include/cmb_b200.h``) and the C++ CLI
 it (``build``); there is no Python or CPU fallback for any probe.
 """
 
-from .capi import CmbError, lib, check, library_path  # noqa: F401
-
 __all__ = ["CmbError", "lib", "check", "library_path"]
+
+
+def __getattr__(name):
+    # The library loads on first use of any of these names, so that
+    # `python -m cuda_micro_bench_b200.build` works before it exists; using
+    # them without the built library raises ImportError (no fallback).
+    if name in __all__:
+        from . import capi
+
+        return getattr(capi, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
