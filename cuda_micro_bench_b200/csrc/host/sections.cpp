@@ -52,24 +52,37 @@ struct DevBuf {
 // Milliseconds of each of `runs` launches of fn (CUDA events on the legacy
 // default stream); returns the median after dropping the first `drop`
 // (src/mem_global.cu:42-53 drops one of six and takes the median of five).
+// A pair of timing events, destroyed on every return path.
+struct EventPair {
+  cudaEvent_t a = nullptr, b = nullptr;
+  EventPair() = default;
+  EventPair(const EventPair &) = delete;
+  ~EventPair() {
+    if (a != nullptr) cudaEventDestroy(a);
+    if (b != nullptr) cudaEventDestroy(b);
+  }
+  int create() {
+    CMB_CUDA_TRY(cudaEventCreate(&a));
+    CMB_CUDA_TRY(cudaEventCreate(&b));
+    return CMB_OK;
+  }
+};
+
 template <class F>
 int time_median(F fn, int runs, int drop, double *ms_out) {
-  cudaEvent_t a, b;
-  CMB_CUDA_TRY(cudaEventCreate(&a));
-  CMB_CUDA_TRY(cudaEventCreate(&b));
+  EventPair ev;
+  TRY(ev.create());
   std::vector<double> ms;
   for (int r = 0; r < runs; ++r) {
-    CMB_CUDA_TRY(cudaEventRecord(a, nullptr));
-    const int rc = fn();
-    if (rc != CMB_OK) return rc;
-    CMB_CUDA_TRY(cudaEventRecord(b, nullptr));
-    CMB_CUDA_TRY(cudaEventSynchronize(b));
+    CMB_CUDA_TRY(cudaEventRecord(ev.a, nullptr));
+    TRY(fn());
+    CMB_CUDA_TRY(cudaEventRecord(ev.b, nullptr));
+    CMB_CUDA_TRY(cudaEventSynchronize(ev.b));
     float t = 0.f;
-    CMB_CUDA_TRY(cudaEventElapsedTime(&t, a, b));
+    CMB_CUDA_TRY(cudaEventElapsedTime(&t, ev.a, ev.b));
     if (r >= drop) ms.push_back(t);
   }
-  cudaEventDestroy(a);
-  cudaEventDestroy(b);
+  if (ms.empty()) return fail(CMB_ERR_INVALID_ARG, "time_median: %d runs, %d dropped", runs, drop);
   std::sort(ms.begin(), ms.end());
   *ms_out = ms[ms.size() / 2];
   return CMB_OK;
