@@ -59,8 +59,10 @@ def test_cli_full_run(cuda, tmp_path):
     assert v("memory_more", "l2_aggregate_verified") == 1.0
     assert v("memory_more", "l2_aggregate_bw_gbps") > v("memory", "dram_read_bw_gbps")
     assert 5 < v("pcie", "htod_bandwidth_GiB_s") < 128 and 5 < v("pcie", "dtoh_bandwidth_GiB_s") < 128
-    from cuda_micro_bench_b200 import validate_results
+    from cuda_micro_bench_b200 import compare, validate_results
     assert validate_results.check(doc) == []
+    table = compare.markdown(doc)
+    assert "tcgen05 GEMM" in table and "n/a" not in table.split("NVLink")[0]
     print(p.stdout)
 
 
