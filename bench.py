@@ -443,6 +443,18 @@ def probe_tma(torch, stream, sh, peaks):
                       "frac_of_8tbs_spec": round(gbs / 8000.0, 4), "stages": stages, "box": [128, 128],
                       "bit_exact": bool(torch.equal(src, dst)), "status": int(status.item()),
                       "ms": round(ms, 4)}
+    # TMA loads with load/store-unit stores (the stage frees once read into
+    # registers), 3 stages x 2 CTAs per SM
+    fn = lambda: check("cmb_tma_tile_copy_tuned", ctypes.c_void_p(dst.data_ptr()),
+                       ctypes.c_void_p(src.data_ptr()), n, n, 128, 128, 3, 2, 4,
+                       ctypes.c_void_p(status.data_ptr()), sh)
+    dst.zero_()
+    ms = _median_ms(torch, stream, fn)
+    gbs = 2.0 * 2 * n * n / (ms * 1e-3) / 1e9
+    out["tile_copy_tma_load_lsu_store"] = {
+        "GB/s": round(gbs, 2), "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+        "stages": 3, "ctas_per_sm": 2, "box": [128, 128], "bit_exact": bool(torch.equal(src, dst)),
+        "status": int(status.item()), "ms": round(ms, 4)}
     fn = lambda: check("cmb_tma_tile_load_bf16", ctypes.c_void_p(src.data_ptr()), n, n, 128, 128,
                        4, ctypes.c_void_p(xor.data_ptr()), 4096,
                        ctypes.c_void_p(status.data_ptr()), sh)

@@ -201,6 +201,116 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
 }
 
+// TMA loads with load/store-unit stores: warp 0 fills the ring as above;
+// kLsuStoreWarps warps copy each tile from shared memory into registers
+// (16-byte vectors, consecutive threads on consecutive vectors of a row),
+// hand the stage back as soon as their shared-memory reads are done, then
+// write the registers out with streaming 16-byte stores, clipped at the
+// matrix edge.  The stage is free before the stores complete, unlike a TMA
+// store, which holds it until the store has read it.
+constexpr int kLsuStoreWarps = 4;
+constexpr int kLsuThreads = 32 * (1 + kLsuStoreWarps);
+constexpr int kLsuVecs = 16;  // vectors per thread per round (one 32 KiB tile)
+
+template <int STAGES>
+__global__ void __launch_bounds__(kLsuThreads)
+    k_tma_tile_copy_lsu(const __grid_constant__ CUtensorMap src_map, TileShape shape,
+                        uint32_t tile_bytes, char *__restrict__ dst, int *status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
+  __shared__ int abort_flag, loads_issued, tiles_consumed;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      dev::mbar_init(dev::smem_addr(&full[s]), 1);
+      dev::mbar_init(dev::smem_addr(&empty[s]), kLsuStoreWarps);
+    }
+    abort_flag = 0;
+    loads_issued = 0;
+    tiles_consumed = 0;
+    dev::fence_mbar_init();
+    dev::tma_prefetch_desc(&src_map);
+  }
+  __syncthreads();
+  const int my_tiles = tiles_of(shape);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int k = 0;
+      for (; k < my_tiles; ++k) {
+        const int s = k % STAGES, use = k / STAGES;
+        if (use > 0 && !dev::mbar_wait_bounded(dev::smem_addr(&empty[s]), (use - 1) & 1)) {
+          dev::report_status(status, CMB_ERR_TIMEOUT);
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        if (*(volatile int *)&abort_flag) break;
+        const int t = tile_of(shape, k);
+        const int ty = t / shape.tiles_x, tx = t - ty * shape.tiles_x;
+        const uint32_t bar = dev::smem_addr(&full[s]);
+        dev::mbar_arrive_expect_tx(bar, tile_bytes);
+        dev::tma_load_2d(dev::smem_addr(ring + (size_t)s * tile_bytes), &src_map,
+                         tx * shape.box_cols, ty * shape.box_rows, bar);
+      }
+      loads_issued = k;
+    }
+  } else {
+    const int t = threadIdx.x - 32;                // 0 .. 32 * kLsuStoreWarps - 1
+    constexpr int kT = 32 * kLsuStoreWarps;
+    const int vpr = shape.box_cols / 8;            // 16-byte vectors per tile row
+    const int nvec = static_cast<int>(tile_bytes / 16);
+    int k = 0;
+    for (; k < my_tiles; ++k) {
+      const int s = k % STAGES;
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), (k / STAGES) & 1) ||
+          *(volatile int *)&abort_flag) {
+        dev::report_status(status, CMB_ERR_TIMEOUT);
+        atomicExch(&abort_flag, 1);
+        break;
+      }
+      const int tile = tile_of(shape, k);
+      const int ty = tile / shape.tiles_x, tx = tile - ty * shape.tiles_x;
+      const int row0 = ty * shape.box_rows, col0 = tx * shape.box_cols;
+      const uint4 *buf = reinterpret_cast<const uint4 *>(ring + (size_t)s * tile_bytes);
+      for (int base = 0; base < nvec; base += kT * kLsuVecs) {
+        uint4 v[kLsuVecs];
+#pragma unroll
+        for (int j = 0; j < kLsuVecs; ++j) {
+          const int i = base + j * kT + t;
+          if (i < nvec) v[j] = buf[i];
+        }
+        if (base + kT * kLsuVecs >= nvec) {
+          // every read of this stage by this warp is done: hand it back
+          __syncwarp();
+          if (lane == 0) dev::mbar_arrive(dev::smem_addr(&empty[s]));
+        }
+#pragma unroll
+        for (int j = 0; j < kLsuVecs; ++j) {
+          const int i = base + j * kT + t;
+          if (i >= nvec) continue;
+          const int r = i / vpr, c = i - r * vpr;
+          const int grow = row0 + r, gcol = col0 + c * 8;
+          if (grow < shape.rows && gcol < shape.cols)
+            dev::st_stream_v4(dst + ((size_t)grow * shape.cols + gcol) * 2, v[j]);
+        }
+      }
+    }
+    if (t == 0) tiles_consumed = k;
+  }
+  __syncthreads();
+  // After a failed wait: wait (bounded) for loads still in flight into the
+  // ring before the CTA's shared memory goes away.
+  if (threadIdx.x == 0 && tiles_consumed < loads_issued) {
+    for (int k = tiles_consumed; k < loads_issued; ++k) {
+      const int s = k % STAGES;
+      if (!dev::mbar_wait_bounded(dev::smem_addr(&full[s]), (k / STAGES) & 1, 100000000ull))
+        break;
+    }
+  }
+}
+
 __global__ void k_tma_1d_latency(const __grid_constant__ CUtensorMap map, int iters,
                                  uint32_t *out_cycles, int *status) {
   __shared__ __align__(128) uint8_t buf[128];
@@ -225,6 +335,19 @@ __global__ void k_tma_1d_latency(const __grid_constant__ CUtensorMap map, int it
   }
   const uint64_t t1 = dev::clock64_after(done + buf[0]);
   *out_cycles = static_cast<uint32_t>(t1 - t0);
+}
+
+template <int STAGES>
+int launch_tile_lsu(const CUtensorMap &sm, TileShape shape, uint32_t tile_bytes, void *dst,
+                    int *status, cudaStream_t stream, int grid) {
+  const size_t smem = (size_t)STAGES * tile_bytes + 1024;
+  auto kern = k_tma_tile_copy_lsu<STAGES>;
+  CMB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  kern<<<grid, kLsuThreads, smem, stream>>>(sm, shape, tile_bytes, static_cast<char *>(dst),
+                                            status);
+  CMB_LAUNCH_CHECK();
+  return CMB_OK;
 }
 
 template <int STAGES, bool kStore>
@@ -285,8 +408,10 @@ int tile_impl(void *dst, const void *src, int rows, int cols, int box_rows, int 
   int grid = grid_override > 0 ? grid_override : current_sm_count() * ctas_per_sm;
   if (grid > shape.tiles) grid = shape.tiles;
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
+  const bool lsu_stores = store && (contiguous & 4);
 #define CMB_TILE_CASE(S)                                                                      \
   case S:                                                                                     \
+    if (lsu_stores) return launch_tile_lsu<S>(sm, shape, tile_bytes, dst, status, stream, grid); \
     return store ? launch_tile<S, true>(sm, dm, shape, tile_bytes, ctas_per_sm, status,       \
                                         xor_out, stream, grid)                                \
                  : launch_tile<S, false>(sm, dm, shape, tile_bytes, ctas_per_sm, status,      \

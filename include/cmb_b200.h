@@ -168,7 +168,9 @@ int cmb_tma_tile_copy_bf16(void *dst, const void *src, int rows, int cols, int b
 /* cmb_tma_tile_copy_bf16 with placement options, for sweeps: flags bit 0 =
  * give each CTA one contiguous run of tiles (default: CTA b strides over
  * tiles b, b + grid, ... in row-major tile order); bit 1 = L2 evict-first
- * policy on the loads and stores. */
+ * policy on the loads and stores (TMA stores only); bit 2 = write the tiles
+ * with load/store-unit stores from 4 warps instead of TMA stores (the stage
+ * returns to the loads once read into registers). */
 int cmb_tma_tile_copy_tuned(void *dst, const void *src, int rows, int cols, int box_rows,
                             int box_cols, int stages, int ctas_per_sm, int flags, int *status,
                             cmb_stream_t stream);

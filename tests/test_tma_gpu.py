@@ -12,11 +12,15 @@ from tests.helpers import dptr, stream_handle
 pytestmark = pytest.mark.gpu
 
 
-def _copy(cuda, cmb, src, rows, cols, box=(128, 128), stages=4, ctas=1, guard=256):
+def _copy(cuda, cmb, src, rows, cols, box=(128, 128), stages=4, ctas=1, guard=256, flags=None):
     dst = cuda.zeros(rows * cols + guard, dtype=cuda.int16, device="cuda")
     status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
-    cmb.check("cmb_tma_tile_copy_bf16", dptr(dst), dptr(src), rows, cols, box[0], box[1], stages,
-              ctas, dptr(status), stream_handle(cuda))
+    if flags is None:
+        cmb.check("cmb_tma_tile_copy_bf16", dptr(dst), dptr(src), rows, cols, box[0], box[1],
+                  stages, ctas, dptr(status), stream_handle(cuda))
+    else:
+        cmb.check("cmb_tma_tile_copy_tuned", dptr(dst), dptr(src), rows, cols, box[0], box[1],
+                  stages, ctas, flags, dptr(status), stream_handle(cuda))
     cuda.cuda.synchronize()
     assert int(status.item()) == 0
     return dst
@@ -35,6 +39,24 @@ def test_tile_copy_bit_exact(cuda, cmb, rows, cols, box, stages, ctas):
     dst = _copy(cuda, cmb, src, rows, cols, box, stages, ctas)
     assert cuda.equal(dst[: rows * cols], src)
     assert int(dst[rows * cols:].count_nonzero()) == 0  # nothing past the matrix
+
+
+@pytest.mark.parametrize("flags", [1, 2, 4, 5])
+@pytest.mark.parametrize("rows,cols,box,stages,ctas", [
+    (256, 256, (128, 128), 4, 1),
+    (200, 136, (128, 128), 4, 2),      # ragged: partial tiles on both edges
+    (1000, 1024, (64, 256), 2, 2),
+    (777, 520, (32, 128), 8, 1),
+    (3, 8, (128, 128), 3, 1),
+    (4099, 4104, (256, 64), 3, 2),
+])
+def test_tile_copy_options_bit_exact(cuda, cmb, rows, cols, box, stages, ctas, flags):
+    """Contiguous tile runs (bit 0), evict-first (bit 1), load/store-unit
+    stores (bit 2), and bits 0 + 2 together."""
+    src = cuda.randint(-32768, 32767, (rows * cols,), dtype=cuda.int16, device="cuda")
+    dst = _copy(cuda, cmb, src, rows, cols, box, stages, ctas, flags=flags)
+    assert cuda.equal(dst[: rows * cols], src)
+    assert int(dst[rows * cols:].count_nonzero()) == 0
 
 
 def test_tile_copy_full_size(cuda, cmb):
