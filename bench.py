@@ -763,7 +763,11 @@ def main(argv=None) -> int:
                     help="run only this probe (repeatable); no headline line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
-        ap.error("--warmup must be >= 3")
+        # at least 3 untimed warm-up steps always run; the line reports the count used
+        log(f"--warmup {args.warmup} raised to 3")
+        args.warmup = 3
+    if args.steps < 1:
+        ap.error("--steps must be >= 1")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.gpus != world:
         ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")

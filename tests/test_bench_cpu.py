@@ -38,8 +38,15 @@ def test_reference_arm_other_ranks_exit_quietly():
     assert p.returncode == 0 and p.stdout.strip() == ""
 
 
+def test_warmup_is_raised_to_three():
+    p = _run("--impl", "reference", "--steps", "2", "--warmup", "1")
+    assert p.returncode == 0, p.stderr
+    assert json.loads(p.stdout.strip().splitlines()[-1])["warmup"] == 3
+    assert "raised to 3" in p.stderr
+
+
 def test_argument_checks():
-    p = _run("--warmup", "2")
-    assert p.returncode != 0 and "--warmup must be >= 3" in p.stderr
+    p = _run("--steps", "0")
+    assert p.returncode != 0 and "--steps must be >= 1" in p.stderr
     p = _run("--gpus", "2")
     assert p.returncode != 0 and "torchrun" in p.stderr
