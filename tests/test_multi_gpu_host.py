@@ -8,6 +8,8 @@ import socket
 
 import numpy as np
 import pytest
+from hypothesis import given, settings
+from hypothesis import strategies as st
 
 from cuda_micro_bench_b200 import multi_gpu
 
@@ -34,6 +36,26 @@ def test_plans_deliver_every_byte_once(mode, world):
         for s in multi_gpu.sources(mode, r, world, nbytes):
             got = recv[r][s.recv_off:s.recv_off + s.nbytes]
             assert np.array_equal(got, send[s.src_rank][s.src_off:s.src_off + s.nbytes])
+
+
+@settings(max_examples=60, deadline=None)
+@given(st.sampled_from(["ring", "alltoall"]), st.integers(min_value=1, max_value=8),
+       st.integers(min_value=1, max_value=64))
+def test_plans_any_world_and_size(mode, world, units):
+    """Every receive byte written once, from the byte the plan names, for
+    any world size and any size the plan accepts (16-byte chunks)."""
+    nbytes = 16 * world * units
+    send, recv, written = _simulate(mode, world, nbytes)
+    total_egress = 0
+    for r in range(world):
+        assert np.all(written[r] == 1)
+        for s in multi_gpu.sources(mode, r, world, nbytes):
+            assert np.array_equal(recv[r][s.recv_off:s.recv_off + s.nbytes],
+                                  send[s.src_rank][s.src_off:s.src_off + s.nbytes])
+        total_egress += multi_gpu.egress_bytes(mode, r, world, nbytes)
+    # bytes that cross between GPUs: all of them on a ring of 2+, (N-1)/N of them all-to-all
+    expect = (world * nbytes if world > 1 else 0) if mode == "ring" else (world - 1) * nbytes
+    assert total_egress == expect
 
 
 def test_egress_bytes():
