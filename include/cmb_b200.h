@@ -99,8 +99,8 @@ int cmb_stream_sum_f32(const float *src, size_t n, double *out_sum, void *worksp
  * a GPU that would need more returns CMB_ERR_INVALID_ARG.  Nothing is
  * allocated: no cudaMalloc, cudaFree or allocating library call.
  * The first call on a device looks up the array's device address (once per
- * device, with that device current); make that first call before any stream
- * capture.  All calls on a device share the array: calls that overlap on
+ * device, with that device current).  All calls on a device share the
+ * array: calls that overlap on
  * the GPU (other streams, or other host threads) race and give wrong sums;
  * serialise them.  The result equals cmb_stream_sum_f32's for the same
  * input. */
