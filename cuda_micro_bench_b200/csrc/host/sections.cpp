@@ -904,9 +904,9 @@ const Section kSections[] = {
 
 void usage(const char *name) {
   printf("Usage: %s [option]...\nOptions:\n", name);
-  for (const auto &s : kSections) printf("  %-12s %s\n", s.flag, s.help);
-  printf("  %-12s %s\n", "--json", "Run all sections and write the results file");
-  printf("  %-12s %s\n", "--all", "Run all sections (default)");
+  for (const auto &s : kSections) printf("  %-14s %s\n", s.flag, s.help);
+  printf("  %-14s %s\n", "--json", "Run all sections and write the results file");
+  printf("  %-14s %s\n", "--all", "Run all sections (default)");
 }
 
 // Runs one section inside an NVTX range named by its flag, so a profiler's
