@@ -20,14 +20,23 @@ int current_sm_count();
 // Compute capability major*10+minor of the current device.
 int current_cc();
 
+// The source file's name without its directories (error messages name the
+// file, not the machine it was built on).
+inline const char *source_name(const char *path) {
+  const char *base = path;
+  for (const char *p = path; *p != '\0'; ++p)
+    if (*p == '/') base = p + 1;
+  return base;
+}
+
 }  // namespace cmb
 
 #define CMB_CUDA_TRY(call)                                                              \
   do {                                                                                  \
     cudaError_t e_ = (call);                                                            \
     if (e_ != cudaSuccess)                                                              \
-      return ::cmb::fail(CMB_ERR_CUDA, "%s:%d: %s: %s", __FILE__, __LINE__, #call,      \
-                         cudaGetErrorString(e_));                                       \
+      return ::cmb::fail(CMB_ERR_CUDA, "%s:%d: %s: %s", ::cmb::source_name(__FILE__),   \
+                         __LINE__, #call, cudaGetErrorString(e_));                      \
   } while (0)
 
 // Checks the launch that was just enqueued.
