@@ -8,9 +8,11 @@
 //
 // Sum: the same loop; each loaded vector is summed pairwise in fp32 and
 // added to one of UNROLL fp64 accumulators per thread, which are combined
-// per CTA in fp64; each CTA writes one fp64 partial to the workspace, and
-// the last CTA to finish (atomic ticket) adds the partials in CTA order, so
-// the result does not depend on CTA scheduling.
+// per CTA in fp64; each CTA writes one fp64 partial to the workspace, and a
+// one-CTA combine kernel, launched behind the sum with programmatic stream
+// serialization (its launch overlaps the sum; it waits for the sum grid to
+// complete), adds the partials in CTA order, so the result does not depend
+// on CTA scheduling and nothing in the workspace needs clearing first.
 #include "cmb_device.cuh"
 #include "cmb_host.h"
 
@@ -103,9 +105,8 @@ __global__ void k_copy_bytes(char *__restrict__ dst, const char *__restrict__ sr
 }
 
 struct SumWorkspace {
-  unsigned int ticket;   // CTAs finished so far in this launch
-  unsigned int pad[63];  // keeps the partials on their own 256-byte line
-  double partial[1];     // one per CTA
+  unsigned int reserved[64];  // header (256 bytes); keeps the partials on their own lines
+  double partial[1];          // one per CTA
 };
 
 __device__ __forceinline__ double block_sum_f64(double v, double *smem) {
@@ -122,12 +123,16 @@ __device__ __forceinline__ double block_sum_f64(double v, double *smem) {
   return r;  // valid in warp 0
 }
 
-// Sums src[0:n).  `head` floats before the first 16-byte boundary and the
-// tail after the last whole vector are added by CTA 0.
+// Sums src[0:n) into one fp64 partial per CTA.  `head` floats before the
+// first 16-byte boundary and the tail after the last whole vector are added
+// by CTA 0.  The kernel lets its dependent (k_sum_combine, launched with
+// programmatic stream serialization) start at once; that kernel waits for
+// this grid to finish before it reads the partials.
 template <int VB, int UNROLL>
 __global__ void __launch_bounds__(kStreamThreads) k_stream_sum(const float *__restrict__ src,
                                                                size_t n, size_t head,
-                                                               SumWorkspace *ws, double *out) {
+                                                               SumWorkspace *ws) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int F = VB / 4;  // floats per vector
   const float *body = src + head;
   const size_t nvec = (n - head) / F;
@@ -166,28 +171,22 @@ __global__ void __launch_bounds__(kStreamThreads) k_stream_sum(const float *__re
     for (size_t i = threadIdx.x; i < head; i += kStreamThreads) t += src[i];
     for (size_t i = head + nvec * F + threadIdx.x; i < n; i += kStreamThreads) t += src[i];
   }
-
   __shared__ double red[kStreamThreads / 32];
-  __shared__ bool last;
-  double b = block_sum_f64(t, red);
-  if (threadIdx.x == 0) {
-    ws->partial[blockIdx.x] = b;
-    __threadfence();
-    unsigned int done = atomicAdd(&ws->ticket, 1u);
-    last = (done == gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!last) return;
-  // Last CTA: fixed-order combine of all partials.
-  __threadfence();
+  const double b = block_sum_f64(t, red);
+  if (threadIdx.x == 0) ws->partial[blockIdx.x] = b;
+}
+
+// Fixed-order combine of the per-CTA partials (deterministic sums).  Its
+// griddepcontrol.wait returns once the sum grid has completed and its
+// writes are visible.
+__global__ void __launch_bounds__(kStreamThreads) k_sum_combine(const SumWorkspace *ws,
+                                                                int parts, double *out) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   double s = 0.0;
-  for (unsigned int i = threadIdx.x; i < gridDim.x; i += kStreamThreads)
-    s += __ldcg(&ws->partial[i]);
+  for (int i = threadIdx.x; i < parts; i += kStreamThreads) s += ws->partial[i];
+  __shared__ double red[kStreamThreads / 32];
   s = block_sum_f64(s, red);
-  if (threadIdx.x == 0) {
-    *out = s;
-    ws->ticket = 0;  // leave the workspace ready for the next launch
-  }
+  if (threadIdx.x == 0) *out = s;
 }
 
 struct CopyConfig {
@@ -260,12 +259,24 @@ int stream_sum_launch(const float *src, size_t n, double *out, void *ws, int max
   int grid = stream_grid(nvec, (size_t)kStreamThreads * kSumUnroll, kSumCtasPerSm);
   if (grid > max_grid) grid = max_grid;
   SumWorkspace *w = static_cast<SumWorkspace *>(ws);
-  CMB_CUDA_TRY(cudaMemsetAsync(&w->ticket, 0, sizeof(unsigned int), stream));
   if (((reinterpret_cast<uintptr_t>(src) + h * 4) & 31) == 0)
-    k_stream_sum<32, kSumUnroll><<<grid, kStreamThreads, 0, stream>>>(src, n, h, w, out);
+    k_stream_sum<32, kSumUnroll><<<grid, kStreamThreads, 0, stream>>>(src, n, h, w);
   else
-    k_stream_sum<16, kSumUnroll><<<grid, kStreamThreads, 0, stream>>>(src, n, h, w, out);
+    k_stream_sum<16, kSumUnroll><<<grid, kStreamThreads, 0, stream>>>(src, n, h, w);
   CMB_LAUNCH_CHECK();
+  // The combine is launched behind the sum with programmatic stream
+  // serialization, so its launch overlaps the sum instead of following it.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CMB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_sum_combine, static_cast<const SumWorkspace *>(w), grid,
+                                  out));
   return CMB_OK;
 }
 

@@ -1,8 +1,8 @@
 // stream_noalloc.cu — the read-stream sum for callers that cannot allocate
 // device memory.
 //
-// cmb_stream_sum_f32 needs a caller-allocated workspace (one fp64 partial
-// per CTA plus a finish counter).  Some callers cannot call cudaMalloc: code
+// cmb_stream_sum_f32 needs a caller-allocated workspace (a 256-byte header
+// and one fp64 partial per CTA).  Some callers cannot call cudaMalloc: code
 // whose device memory is all owned by another allocator (a framework's
 // caching allocator or a fixed arena), or latency-critical paths that cannot
 // afford cudaMalloc/cudaFree, which may synchronise the device.  For them,
@@ -83,7 +83,6 @@ extern "C" int cmb_stream_sum_f32_noalloc(const float *src, size_t n, double *ou
   int err = CMB_OK;
   void *scratch = scratch_address_for_current_device(&err);
   if (scratch == nullptr) return err;
-  // stream_sum_launch clears the finish counter before the kernel runs; the
-  // partials are written before they are read, so nothing else needs zeroing.
+  // The partials are written before they are read, so nothing needs zeroing.
   return stream_sum_launch(src, n, out_sum, scratch, max_grid, stream);
 }
