@@ -151,6 +151,22 @@ def test_sum_past_4gib(cuda, cmb, orc):
     assert abs(got - ref) <= REL_TOL_SUM * max(abs(ref), 1.0), (got, ref)
 
 
+@pytest.mark.parametrize("n", [1000, (1 << 22) + 3, 1 << 28])
+def test_sum_reads_only_this_calls_partials(cuda, cmb, orc, n):
+    """A workspace full of NaN bytes before one call: the combine must read
+    only the partials this call's sum grid wrote (it waits for that grid)."""
+    d = cuda.empty(n, dtype=cuda.float32, device="cuda")
+    cmb.check("cmb_fill_uniform_f32", dptr(d), n, ctypes.c_uint64(n), stream_handle(cuda))
+    ws_bytes = cmb.lib.cmb_stream_sum_workspace_bytes(n)
+    ws = cuda.full((ws_bytes,), 0xFF, dtype=cuda.uint8, device="cuda")
+    out = cuda.full((1,), float("nan"), dtype=cuda.float64, device="cuda")
+    cmb.check("cmb_stream_sum_f32", dptr(d), n, dptr(out), dptr(ws), ws_bytes, stream_handle(cuda))
+    got = float(out.item())
+    host = d.cpu().numpy()
+    ref = orc.orc_sum_f64(ptr(host), n, 0)
+    assert abs(got - ref) <= REL_TOL_SUM * max(abs(ref), 1.0), (got, ref)
+
+
 def test_sum_rejects_small_workspace(cuda, cmb):
     d = cuda.zeros(1024, dtype=cuda.float32, device="cuda")
     ws = cuda.empty(16, dtype=cuda.uint8, device="cuda")
