@@ -186,7 +186,8 @@ def test_copy_host_buffers(cuda, cmb):
     assert np.array_equal(src, dst)
 
 
-@pytest.mark.parametrize("nbytes,passes,ctas", [(16, 1, 1), (8 << 20, 4, 0), ((1 << 20) + 48, 3, 7)])
+@pytest.mark.parametrize("nbytes,passes,ctas", [(16, 1, 1), (8 << 20, 4, 0), ((1 << 20) + 48, 3, 7),
+                                                (48, 1000, 2), (64 << 10, 37, 0)])
 def test_l2_read_exact_sum(cuda, cmb, orc, nbytes, passes, ctas):
     words = nbytes // 4
     d = cuda.empty(words, dtype=cuda.int32, device="cuda")
