@@ -83,7 +83,11 @@ size_t cmb_stream_sum_workspace_bytes(size_t n);
  * partials, fp64 block and grid combine, fixed order).  Replaces the
  * read-only stream kernel_stream_read (src/mem_global.cu:17-26,47), whose
  * XOR sink is replaced by a checkable sum.  `workspace` is device memory of
- * cmb_stream_sum_workspace_bytes(n) bytes; it needs no initialisation. */
+ * cmb_stream_sum_workspace_bytes(n) bytes; it needs no initialisation.
+ * Two calls whose work overlaps on the GPU need separate workspaces.  The
+ * call enqueues two kernels: the sum, and a one-CTA combine launched with
+ * programmatic stream serialization that writes *out_sum once the sum grid
+ * has completed. */
 int cmb_stream_sum_f32(const float *src, size_t n, double *out_sum, void *workspace,
                        size_t workspace_bytes, cmb_stream_t stream);
 
