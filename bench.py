@@ -278,7 +278,7 @@ def run_ours(args) -> int:
         "config": {"workload": f"stream_copy: fp32[{n}] ({nbytes / 2**30:g} GiB) -> second "
                                "buffer per GPU, sharded, no exchange",
                    "bytes_per_gpu_per_step": 2 * nbytes, "parallelism": f"shard{ranks.world}",
-                   "l2": "inputs larger than L2 (4 GiB vs 126 MB)", "impl": "ours"},
+                   "l2": f"inputs larger than L2 ({nbytes / 2**30:g} GiB vs 126 MB)", "impl": "ours"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps,
         "clocks": clk,
     }
