@@ -62,24 +62,34 @@ extern "C" int cmb_stream_copy_host(void *host_dst, const void *host_src, size_t
   const char *hs = static_cast<const char *>(host_src);
   char *hd = static_cast<char *>(host_dst);
   const size_t nchunks = (bytes + chunk - 1) / chunk;
-  for (size_t c = 0; c < nchunks; ++c) {
-    const int k = static_cast<int>(c % slots);
-    const size_t off = c * chunk, len = off + chunk <= bytes ? chunk : bytes - off;
-    if (c >= (size_t)slots) CMB_CUDA_TRY(cudaStreamWaitEvent(s->h2d, s->in_free[k], 0));
-    CMB_CUDA_TRY(cudaMemcpyAsync(a + k * chunk, hs + off, len, cudaMemcpyHostToDevice, s->h2d));
-    CMB_CUDA_TRY(cudaEventRecord(s->in_ready[k], s->h2d));
-    CMB_CUDA_TRY(cudaStreamWaitEvent(s->comp, s->in_ready[k], 0));
-    if (c >= (size_t)slots) CMB_CUDA_TRY(cudaStreamWaitEvent(s->comp, s->out_free[k], 0));
-    int rc = cmb_stream_copy(b + k * chunk, a + k * chunk, len, s->comp);
-    if (rc != CMB_OK) return rc;
-    CMB_CUDA_TRY(cudaEventRecord(s->in_free[k], s->comp));
-    CMB_CUDA_TRY(cudaEventRecord(s->out_ready[k], s->comp));
-    CMB_CUDA_TRY(cudaStreamWaitEvent(s->d2h, s->out_ready[k], 0));
-    CMB_CUDA_TRY(cudaMemcpyAsync(hd + off, b + k * chunk, len, cudaMemcpyDeviceToHost, s->d2h));
-    CMB_CUDA_TRY(cudaEventRecord(s->out_free[k], s->d2h));
-  }
-  CMB_CUDA_TRY(cudaStreamSynchronize(s->d2h));
-  CMB_CUDA_TRY(cudaStreamSynchronize(s->comp));
-  CMB_CUDA_TRY(cudaStreamSynchronize(s->h2d));
+  const auto enqueue = [&]() -> int {
+    for (size_t c = 0; c < nchunks; ++c) {
+      const int k = static_cast<int>(c % slots);
+      const size_t off = c * chunk, len = off + chunk <= bytes ? chunk : bytes - off;
+      if (c >= (size_t)slots) CMB_CUDA_TRY(cudaStreamWaitEvent(s->h2d, s->in_free[k], 0));
+      CMB_CUDA_TRY(cudaMemcpyAsync(a + k * chunk, hs + off, len, cudaMemcpyHostToDevice, s->h2d));
+      CMB_CUDA_TRY(cudaEventRecord(s->in_ready[k], s->h2d));
+      CMB_CUDA_TRY(cudaStreamWaitEvent(s->comp, s->in_ready[k], 0));
+      if (c >= (size_t)slots) CMB_CUDA_TRY(cudaStreamWaitEvent(s->comp, s->out_free[k], 0));
+      int rc = cmb_stream_copy(b + k * chunk, a + k * chunk, len, s->comp);
+      if (rc != CMB_OK) return rc;
+      CMB_CUDA_TRY(cudaEventRecord(s->in_free[k], s->comp));
+      CMB_CUDA_TRY(cudaEventRecord(s->out_ready[k], s->comp));
+      CMB_CUDA_TRY(cudaStreamWaitEvent(s->d2h, s->out_ready[k], 0));
+      CMB_CUDA_TRY(cudaMemcpyAsync(hd + off, b + k * chunk, len, cudaMemcpyDeviceToHost, s->d2h));
+      CMB_CUDA_TRY(cudaEventRecord(s->out_free[k], s->d2h));
+    }
+    return CMB_OK;
+  };
+  const int rc = enqueue();
+  // Wait for everything enqueued, on success and on failure alike, so the
+  // caller's host buffers are no longer in use when this returns.
+  const cudaError_t e1 = cudaStreamSynchronize(s->d2h), e2 = cudaStreamSynchronize(s->comp),
+                    e3 = cudaStreamSynchronize(s->h2d);
+  if (rc != CMB_OK) return rc;
+  for (cudaError_t e : {e1, e2, e3})
+    if (e != cudaSuccess)
+      return fail(CMB_ERR_CUDA, "cmb_stream_copy_host: cudaStreamSynchronize: %s",
+                  cudaGetErrorString(e));
   return CMB_OK;
 }
