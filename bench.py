@@ -558,7 +558,41 @@ def probe_gemm(torch, stream, sh, peaks):
                       "frac_of_2x_measured_bf16": round(tf / (2 * peaks["bf16_tflops"]), 4),
                       "ms": round(ms, 4), "sampled_tiles_max_rel_err": err,
                       "within_1e-2": err <= 1e-2, "status": int(status.item())}
-    del a8, b8
+    # bf16 C (each fp32 accumulator rounded to nearest even), the output type
+    # of the measured bf16 peak: cmb_gemm_bf16_out, 2-CTA held-epilogue tiles
+    Cb = torch.empty(M * N, dtype=torch.bfloat16, device="cuda")
+    a64 = A.view(M, K).view(torch.bfloat16).double()
+    b64 = B.view(N, K).view(torch.bfloat16).double()
+
+    def sampled_err_b(a_f64, b_f64):
+        Cm = Cb.view(M, N)
+        worst = 0.0
+        for r, c in zip(rows.tolist(), cols.tolist()):
+            ref = a_f64[r:r + 64] @ b_f64[c:c + 64].T
+            got = Cm[r:r + 64, c:c + 64].double()
+            worst = max(worst, float((got - ref).abs().max() / ref.abs().max()))
+        return worst
+
+    for label, fp8, ops, scales, (fa, fb) in (
+            ("bf16_8192_2cta_bf16out", 0, (A, B), (None, None), (a64, b64)),
+            ("fp8_e4m3_8192_2cta_bf16out", 1, (qa, qb),
+             (ctypes.c_void_p(sa.data_ptr()), ctypes.c_void_p(sb.data_ptr())), (a8, b8))):
+        fn = lambda: check("cmb_gemm_bf16_out", ctypes.c_void_p(ops[0].data_ptr()),
+                           ctypes.c_void_p(ops[1].data_ptr()), ctypes.c_void_p(Cb.data_ptr()),
+                           M, N, K, fp8, scales[0], scales[1],
+                           ctypes.c_void_p(status.data_ptr()), sh)
+        ms = _median_ms(torch, stream, fn)
+        tf = flop / (ms * 1e-3) / 1e12
+        err = sampled_err_b(fa, fb)
+        entry = {"TFLOP/s": round(tf, 1), "ms": round(ms, 4), "sampled_tiles_max_rel_err": err,
+                 "within_1e-2": err <= 1e-2, "status": int(status.item())}
+        if fp8:
+            entry["frac_of_4500_spec"] = round(tf / 4500.0, 4)
+        else:
+            entry["frac_of_measured_bf16"] = round(tf / peaks["bf16_tflops"], 4)
+            entry["frac_of_2250_spec"] = round(tf / 2250.0, 4)
+        out[label] = entry
+    del a8, b8, a64, b64
     # cuBLAS on the same operands, fp32 output like the kernels above
     a16, b16 = A.view(M, K).view(torch.bfloat16), B.view(N, K).view(torch.bfloat16)
     f8a, f8b = qa.view(M, K).view(torch.float8_e4m3fn), qb.view(N, K).view(torch.float8_e4m3fn)
@@ -569,6 +603,11 @@ def probe_gemm(torch, stream, sh, peaks):
         ms = _median_ms(torch, stream, lambda: torch._scaled_mm(
             f8a, f8b.t(), scale_a=sa[0], scale_b=sb[0], out_dtype=torch.float32))
         live["e4m3_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+        ms = _median_ms(torch, stream, lambda: torch.mm(a16, b16.t()))
+        live["bf16_bf16out_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+        ms = _median_ms(torch, stream, lambda: torch._scaled_mm(
+            f8a, f8b.t(), scale_a=sa[0], scale_b=sb[0], out_dtype=torch.bfloat16))
+        live["e4m3_bf16out_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
     except (RuntimeError, TypeError) as e:  # an older torch without these forms
         live["error"] = str(e).splitlines()[0][:200]
     if "bf16_TFLOP/s" in live:
@@ -577,9 +616,14 @@ def probe_gemm(torch, stream, sh, peaks):
     if "e4m3_TFLOP/s" in live:
         out["fp8_e4m3_8192_2cta"]["frac_of_live_cublas"] = round(
             out["fp8_e4m3_8192_2cta"]["TFLOP/s"] / live["e4m3_TFLOP/s"], 4)
-    live["what"] = "torch.mm / torch._scaled_mm (cuBLASLt), same operands, fp32 C, timed alongside"
+    for ours, theirs in (("bf16_8192_2cta_bf16out", "bf16_bf16out_TFLOP/s"),
+                         ("fp8_e4m3_8192_2cta_bf16out", "e4m3_bf16out_TFLOP/s")):
+        if theirs in live:
+            out[ours]["frac_of_live_cublas"] = round(out[ours]["TFLOP/s"] / live[theirs], 4)
+    live["what"] = ("torch.mm / torch._scaled_mm (cuBLASLt), same operands, fp32 C (and bf16 C "
+                    "for the *_bf16out keys), timed alongside")
     out["cublas_same_operands"] = live
-    del A, B, C, qa, qb, a16, b16, f8a, f8b
+    del A, B, C, Cb, qa, qb, a16, b16, f8a, f8b
     return out
 
 

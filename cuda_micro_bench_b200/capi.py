@@ -48,6 +48,7 @@ SIGNATURES = {
     "cmb_gemm_bf16": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "cmb_gemm_e4m3": (_i, [_p, _p, _p, _i, _i, _i, _p, _p, _i, _p, _p]),
     "cmb_gemm_tuned": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
+    "cmb_gemm_bf16_out": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p]),
     "cmb_mma_rate": (_i, [_i, _i, _i, _p, _p, _p, _p]),
     "cmb_quantize_e4m3": (_i, [_p, _sz, _p, _p, _p]),
     "cmb_mma_sync_latency": (_i, [_i, _i, _p, _p, _p]),

@@ -37,6 +37,7 @@
 // All waits are bounded; a wait that gives up reports CMB_ERR_TIMEOUT in
 // `status` and every role drains and leaves.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
 #include "cmb_device.cuh"
@@ -98,18 +99,34 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / gsize;
 }
 
+// Two floats rounded to bf16 (nearest even), `lo` in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void st_cs_u4(void *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ void st_cs_f4(float *p, float a, float b, float c, float d) {
   asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
                "f"(d)
                : "memory");
 }
 
-template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW>
+// kBf16Out: C is bf16 (each fp32 accumulator scaled, then rounded to
+// nearest even); held-epilogue configurations only.
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW, bool kBf16Out = false>
 __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-           const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M, int N, int K,
+           const __grid_constant__ CUtensorMap tmC, void *__restrict__ Cv, int M, int N, int K,
            const float *scale_a, const float *scale_b, int group_m, int *status) {
   using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
+  static_assert(!kBf16Out || Cfg::kHeld, "bf16 output needs the held epilogue");
+  float *const C = static_cast<float *>(Cv);
+  __nv_bfloat16 *const Cb = static_cast<__nv_bfloat16 *>(Cv);
   extern __shared__ uint8_t smem_raw[];
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
@@ -373,47 +390,106 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
           if constexpr (CG == 1) dev::mbar_arrive(eb);
           else dev::mbar_arrive_cluster(tc::map_to_cta(eb, 0));
         }
+        if constexpr (kBf16Out) {
+          // bf16 C: two 32 x 64 boxes (128-byte rows) per half, staged with
+          // the same 128-byte swizzle; 16-byte piece p of a row holds
+          // columns 8p .. 8p+7.
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int col0 = tn * Cfg::kTileN + u * Cfg::kBn + h * 128 + 32 * i;
-          if constexpr (kTmaEpi) {
-            // Same 128-byte-swizzled staging as the two-box epilogue; the
-            // one box is rewritten only after the store that last read it.
-            if (row0 < M && col0 < N) {  // warp-uniform
-              if (epi_count != 0) {
-                if (lane == 0) dev::bulk_wait_group_read<0>();
+          for (int i2 = 0; i2 < 2; ++i2) {
+            const int col0 = tn * Cfg::kTileN + u * Cfg::kBn + h * 128 + 64 * i2;
+            uint32_t w[8][4];
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int ci = 2 * i2 + (p >> 2), c = (p & 3) * 8 + 2 * e;
+                w[p][e] = pack_bf16x2(scale * __uint_as_float(r[ci][c]),
+                                      scale * __uint_as_float(r[ci][c + 1]));
+              }
+            if constexpr (kTmaEpi) {
+              if (row0 < M && col0 < N) {  // warp-uniform
+                if (epi_count != 0) {
+                  if (lane == 0) dev::bulk_wait_group_read<0>();
+                  __syncwarp();
+                }
+                const uint32_t rb = dev::smem_addr(box) + lane * 128;
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                  const uint32_t addr = rb + ((static_cast<uint32_t>(p) ^ (lane & 7)) << 4);
+                  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w[p][0]),
+                               "r"(w[p][1]), "r"(w[p][2]), "r"(w[p][3])
+                               : "memory");
+                }
+                dev::fence_proxy_async_smem();
                 __syncwarp();
+                if (lane == 0) {
+                  dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
+                  dev::bulk_commit_group();
+                }
+                ++epi_count;
               }
-              const uint32_t rb = dev::smem_addr(box) + lane * 128;
+            } else if (row < M) {
+              __nv_bfloat16 *brow = Cb + (size_t)row * N;
+              if (vec_ok && (N % 8 == 0) && col0 + 64 <= N) {
 #pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                const uint32_t addr = rb + ((static_cast<uint32_t>(c) ^ (lane & 7)) << 4);
-                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
-                             "f"(scale * __uint_as_float(r[i][4 * c])),
-                             "f"(scale * __uint_as_float(r[i][4 * c + 1])),
-                             "f"(scale * __uint_as_float(r[i][4 * c + 2])),
-                             "f"(scale * __uint_as_float(r[i][4 * c + 3]))
-                             : "memory");
+                for (int p = 0; p < 8; ++p)
+                  st_cs_u4(brow + col0 + 8 * p, w[p][0], w[p][1], w[p][2], w[p][3]);
+              } else {
+#pragma unroll
+                for (int p = 0; p < 8; ++p)
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const int c = col0 + 8 * p + 2 * e;
+                    const uint32_t v = w[p][e];
+                    if (c < N) brow[c] = __ushort_as_bfloat16(static_cast<unsigned short>(v));
+                    if (c + 1 < N) brow[c + 1] = __ushort_as_bfloat16(static_cast<unsigned short>(v >> 16));
+                  }
               }
-              dev::fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
-                dev::bulk_commit_group();
-              }
-              ++epi_count;
             }
-          } else if (row < M) {
-            if (vec_ok && col0 + 32 <= N) {
+          }
+        } else {
 #pragma unroll
-              for (int c = 0; c < 32; c += 4)
-                st_cs_f4(crow + col0 + c, scale * __uint_as_float(r[i][c]),
-                         scale * __uint_as_float(r[i][c + 1]), scale * __uint_as_float(r[i][c + 2]),
-                         scale * __uint_as_float(r[i][c + 3]));
-            } else {
+          for (int i = 0; i < 4; ++i) {
+            const int col0 = tn * Cfg::kTileN + u * Cfg::kBn + h * 128 + 32 * i;
+            if constexpr (kTmaEpi) {
+              // Same 128-byte-swizzled staging as the two-box epilogue; the
+              // one box is rewritten only after the store that last read it.
+              if (row0 < M && col0 < N) {  // warp-uniform
+                if (epi_count != 0) {
+                  if (lane == 0) dev::bulk_wait_group_read<0>();
+                  __syncwarp();
+                }
+                const uint32_t rb = dev::smem_addr(box) + lane * 128;
 #pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (col0 + c < N) crow[col0 + c] = scale * __uint_as_float(r[i][c]);
+                for (int c = 0; c < 8; ++c) {
+                  const uint32_t addr = rb + ((static_cast<uint32_t>(c) ^ (lane & 7)) << 4);
+                  asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
+                               "f"(scale * __uint_as_float(r[i][4 * c])),
+                               "f"(scale * __uint_as_float(r[i][4 * c + 1])),
+                               "f"(scale * __uint_as_float(r[i][4 * c + 2])),
+                               "f"(scale * __uint_as_float(r[i][4 * c + 3]))
+                               : "memory");
+                }
+                dev::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  dev::tma_store_2d(&tmC, col0, row0, dev::smem_addr(box));
+                  dev::bulk_commit_group();
+                }
+                ++epi_count;
+              }
+            } else if (row < M) {
+              if (vec_ok && col0 + 32 <= N) {
+#pragma unroll
+                for (int c = 0; c < 32; c += 4)
+                  st_cs_f4(crow + col0 + c, scale * __uint_as_float(r[i][c]),
+                           scale * __uint_as_float(r[i][c + 1]), scale * __uint_as_float(r[i][c + 2]),
+                           scale * __uint_as_float(r[i][c + 3]));
+              } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                  if (col0 + c < N) crow[col0 + c] = scale * __uint_as_float(r[i][c]);
+              }
             }
           }
         }
@@ -558,8 +634,8 @@ __global__ void k_quantize_e4m3(const __nv_bfloat16 *__restrict__ x, size_t n,
     scale_out[0] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
 }
 
-template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW>
-int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
+template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW, bool kBf16Out = false>
+int launch_gemm(const void *A, const void *B, void *C, int M, int N, int K,
                 const float *scale_a, const float *scale_b, int group_m, int *status,
                 cudaStream_t stream) {
   using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
@@ -573,14 +649,18 @@ int launch_gemm(const void *A, const void *B, float *C, int M, int N, int K,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   CUtensorMap tcm;
-  if constexpr (kTmaEpi) {
+  if constexpr (kTmaEpi && kBf16Out) {
+    rc = make_tmap_2d(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, M, N, (uint64_t)N * 2, 32, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    if (rc) return rc;
+  } else if constexpr (kTmaEpi) {
     rc = make_tmap_2d(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, M, N, (uint64_t)N * 4, 32, 32,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     if (rc) return rc;
   } else {
     tcm = ta;  // unused
   }
-  auto kern = k_gemm<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
+  auto kern = k_gemm<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW, kBf16Out>;
   CMB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(Cfg::kSmem)));
   const int tiles = ((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
@@ -715,6 +795,28 @@ extern "C" int cmb_gemm_e4m3(const void *A, const void *B, float *C, int M, int 
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
   return dispatch_gemm<true>(A, B, C, M, N, K, scale_a, scale_b, cta_group, 0, 0, 0, 0, 0,
                              status, stream);
+}
+
+extern "C" int cmb_gemm_bf16_out(const void *A, const void *B, void *C, int M, int N, int K,
+                                 int fp8, const float *scale_a, const float *scale_b, int *status,
+                                 cmb_stream_t stream) {
+  int rc = gemm_checks("cmb_gemm_bf16_out", A, B, static_cast<const float *>(C), M, N, K,
+                       fp8 ? 1 : 2, 2);
+  if (rc) return rc;
+  if (fp8 && (scale_a == nullptr || scale_b == nullptr))
+    return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_bf16_out: null scale");
+  if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
+  // the TMA-store epilogue when C's row pitch allows a tensor map
+  const bool tma_ok = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+  if (fp8)
+    return tma_ok ? launch_gemm<2, true, 4, true, 2, 8, true>(A, B, C, M, N, K, scale_a, scale_b, 8,
+                                                              status, stream)
+                  : launch_gemm<2, true, 4, false, 2, 8, true>(A, B, C, M, N, K, scale_a, scale_b,
+                                                               8, status, stream);
+  return tma_ok ? launch_gemm<2, false, 4, true, 2, 8, true>(A, B, C, M, N, K, nullptr, nullptr, 8,
+                                                             status, stream)
+                : launch_gemm<2, false, 4, false, 2, 8, true>(A, B, C, M, N, K, nullptr, nullptr, 8,
+                                                              status, stream);
 }
 
 extern "C" int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst,

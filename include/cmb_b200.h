@@ -224,6 +224,15 @@ int cmb_gemm_tuned(const void *A, const void *B, float *C, int M, int N, int K, 
                    const float *scale_a, const float *scale_b, int cta_group, int stages,
                    int group_m, int epilogue, int tile_n, int epi_warps, int *status,
                    cmb_stream_t stream);
+/* cmb_gemm_bf16 (fp8 = 0) or cmb_gemm_e4m3 (fp8 = 1) with a bf16 C: each fp32
+ * accumulator (times *scale_a * *scale_b for e4m3) is rounded to the nearest
+ * bf16, ties to even.  2-CTA 256 x 512 tiles with the held epilogue; TMA
+ * stores of 32 x 64 boxes when N % 8 == 0 and C is 16-byte aligned, direct
+ * stores otherwise.  No reference counterpart (its probes store nothing);
+ * the output type of the measured cuBLAS peak. */
+int cmb_gemm_bf16_out(const void *A, const void *B, void *C, int M, int N, int K, int fp8,
+                      const float *scale_a, const float *scale_b, int *status,
+                      cmb_stream_t stream);
 /* Tensor-pipe ceiling: `ctas` CTAs (one per SM) each issue `iters` rounds of
  * four tcgen05.mma M=128 N=256 (bf16: fp8 = 0, K = 16; e4m3: fp8 = 1,
  * K = 32) on all-ones operands resident in shared memory, into TMEM, with no

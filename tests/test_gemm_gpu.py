@@ -240,3 +240,49 @@ def test_gemm_rejects_bad_args(cuda, cmb):
                                   0, 0, None, s) == 1
     assert cmb.lib.cmb_gemm_tuned(dptr(a), dptr(a), dptr(c), 16, 16, 16, 0, None, None, 1, 4, 0, 2,
                                   512, 0, None, s) == 1
+
+
+@pytest.mark.parametrize("fp8", [0, 1])
+@pytest.mark.parametrize("M,N,K,offset", [
+    (256, 512, 256, 0), (700, 520, 1040, 0), (1000, 700, 512, 0), (4096, 4600, 208, 0),
+    (512, 1024, 512, 8), (8192, 8192, 8192, 0)])
+def test_gemm_bf16_out_is_the_rounded_fp32_result(cuda, cmb, orc, fp8, M, N, K, offset):
+    """bf16 C equals the fp32 C of the same GEMM rounded to nearest-even
+    bf16, bit for bit (same tiles, same accumulation order), and is within
+    the tolerance of the oracle's fp64 product.  N = 700 (N % 8 != 0) and
+    an 8-byte-offset C take the direct-store epilogue."""
+    A = _normal_bf16(cuda, cmb, M, K, 61, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 62, K ** -0.5)
+    C32 = cuda.full((M * N,), float("nan"), dtype=cuda.float32, device="cuda")
+    cb = cuda.full((M * N + 8,), float("nan"), dtype=cuda.bfloat16, device="cuda")
+    Cb = cb[offset // 2: offset // 2 + M * N]
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    if fp8:
+        qa, sa = _quantize(cuda, cmb, A)
+        qb, sb = _quantize(cuda, cmb, B)
+        ops = (dptr(qa), dptr(qb))
+        cmb.check("cmb_gemm_e4m3", *ops, dptr(C32), M, N, K, dptr(sa), dptr(sb), 2, dptr(status),
+                  stream_handle(cuda))
+        cmb.check("cmb_gemm_bf16_out", *ops, dptr(Cb), M, N, K, 1, dptr(sa), dptr(sb),
+                  dptr(status), stream_handle(cuda))
+        a_h, b_h, dt = qa.cpu().numpy(), qb.cpu().numpy(), 1
+        s_a, s_b = float(sa[0].item()), float(sb[0].item())
+    else:
+        ops = (dptr(A), dptr(B))
+        cmb.check("cmb_gemm_bf16", *ops, dptr(C32), M, N, K, 2, dptr(status), stream_handle(cuda))
+        cmb.check("cmb_gemm_bf16_out", *ops, dptr(Cb), M, N, K, 0, None, None, dptr(status),
+                  stream_handle(cuda))
+        a_h, b_h, dt = A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16), 0
+        s_a = s_b = 1.0
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert cuda.equal(Cb.view(cuda.int16), C32.to(cuda.bfloat16).view(cuda.int16))
+    assert cuda.isnan(cb[:offset // 2]).all() and cuda.isnan(cb[offset // 2 + M * N:]).all()
+    out = Cb.float().cpu().numpy().reshape(M, N)
+    if M * N <= 1 << 20:
+        tiles = [(0, 0, M, N)]
+    else:
+        rng = np.random.default_rng(M + N)
+        tiles = [(int(r) * 64, int(c) * 64, 64, 64)
+                 for r, c in zip(rng.integers(0, M // 64, 16), rng.integers(0, N // 64, 16))]
+    _check_tiles(orc, a_h, b_h, out, K, tiles, dtype=dt, sa=s_a, sb=s_b)
