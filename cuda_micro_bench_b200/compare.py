@@ -31,12 +31,16 @@ ROWS = [
         ("mma.sync m16n8k16 issue rate (registers only)", "tensor_core_extended",
          "bf16_m16n8k16_throughput_TFs", 1.0),
         ("tcgen05 GEMM 8192^3 (TMA, TMEM, checked)", "tensor_core_tcgen05",
-         "bf16_gemm_8192_tflops", 1.0)]),
+         "bf16_gemm_8192_tflops", 1.0),
+        ("tcgen05 GEMM 8192^3, bf16 C", "tensor_core_tcgen05", "bf16_gemm_8192_bf16out_tflops",
+         1.0)]),
     ("FP8 e4m3 tensor throughput", "TFLOP/s", [
         ("mma.sync m16n8k32 issue rate (registers only)", "tensor_core_extended",
          "fp8_m16n8k32_throughput_TFs", 1.0),
         ("tcgen05 GEMM 8192^3 (TMA, TMEM, checked)", "tensor_core_tcgen05",
-         "fp8_e4m3_gemm_8192_tflops", 1.0)]),
+         "fp8_e4m3_gemm_8192_tflops", 1.0),
+        ("tcgen05 GEMM 8192^3, bf16 C", "tensor_core_tcgen05",
+         "fp8_e4m3_gemm_8192_bf16out_tflops", 1.0)]),
     ("NVLink ring, egress per GPU", "GB/s", [
         ("SM peer stores", "p2p", "ring_store_link_gbps", 1.0),
         ("SM bulk copies", "p2p", "ring_bulk_link_gbps", 1.0),

@@ -653,6 +653,38 @@ int benchmark_tensor_core_extended() {
     g_results.log("tensor_core_tcgen05", p + "_frac_of_spec", tf / spec, "");
     g_results.log("tensor_core_tcgen05", p + "_max_rel_err", err, "");
     g_results.log("tensor_core_tcgen05", p + "_verified", 1.0, "bool");
+
+    // The same GEMM with bf16 C: timed, and checked to equal the fp32 C
+    // above rounded to nearest-even bf16, element for element.
+    DevBuf cb;
+    TRY(cb.alloc((size_t)M * N * 2));
+    double msb = 0;
+    TRY(time_median(
+        [&] {
+          return cmb_gemm_bf16_out(fp8 ? qa.p : A.p, fp8 ? qb.p : B.p, cb.p, M, N, K, fp8,
+                                   fp8 ? sa.as<float>() : nullptr, fp8 ? sb.as<float>() : nullptr,
+                                   st.as<int>(), nullptr);
+        },
+        6, 1, &msb));
+    CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status != 0) return fail(status, "tcgen05 GEMM (bf16 C): a bounded wait expired");
+    std::vector<uint16_t> hcb((size_t)M * N);
+    CMB_CUDA_TRY(cudaMemcpy(hcb.data(), cb.p, hcb.size() * 2, cudaMemcpyDeviceToHost));
+    size_t bad = 0;
+    for (size_t i = 0; i < hcb.size(); ++i) {
+      uint32_t u;
+      std::memcpy(&u, &hc[i], 4);
+      const uint16_t rne = static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+      bad += hcb[i] != rne;
+    }
+    const double tfb = flop / (msb * 1e-3) / 1e12;
+    printf("  tcgen05 %s GEMM 8192^3, bf16 C: %.1f TFLOP/s, %s\n", fp8 ? "e4m3" : "bf16", tfb,
+           bad == 0 ? "equal to the fp32 C rounded to bf16" : "MISMATCH");
+    if (bad != 0)
+      return fail(CMB_ERR_MISMATCH, "%s: %zu bf16 outputs differ from the rounded fp32 C",
+                  p.c_str(), bad);
+    g_results.log("tensor_core_tcgen05", p + "_bf16out_tflops", tfb, "TFLOP/s");
+    g_results.log("tensor_core_tcgen05", p + "_bf16out_verified", 1.0, "bool");
   }
   return CMB_OK;
 }

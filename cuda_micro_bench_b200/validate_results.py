@@ -150,7 +150,9 @@ def check(doc, full=True, keys=None):
     for p, spec in (("bf16_gemm_8192", B200["bf16_tflops"]),
                     ("fp8_e4m3_gemm_8192", B200["fp8_tflops"])):
         bound("tensor_core_tcgen05", p + "_tflops", 0, spec * 1.05, "dense tensor peak")
+        bound("tensor_core_tcgen05", p + "_bf16out_tflops", 0, spec * 1.05, "dense tensor peak")
         flag("tensor_core_tcgen05", p + "_verified")
+        flag("tensor_core_tcgen05", p + "_bf16out_verified")
         err = val("tensor_core_tcgen05", p + "_max_rel_err")
         if err is not None and err > 1e-2:
             fail(f"tensor_core_tcgen05.{p}_max_rel_err = {err} above 1e-2")

@@ -25,7 +25,7 @@ def test_rows_read_the_reports_keys_and_mark_the_best():
     assert best == "copy engines"
     # rows whose keys the run did not log
     vals, best = rows["BF16 tensor throughput"]
-    assert [v for _, v in vals] == [None, None] and best is None
+    assert [v for _, v in vals] == [None, None, None] and best is None
 
 
 def test_markdown_and_cli(tmp_path, capsys):
