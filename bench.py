@@ -210,6 +210,25 @@ def cpu_memcpy_baseline(sample_bytes: int, steps: int, warmup: int) -> dict:
 # ---------------------------------------------------------------- our arm
 
 
+# Result flags of the probes: a check passed when its flag has this value.
+CHECK_FLAGS = {"bit_exact": True, "within_1e-2": True, "within_1e-5": True,
+               "endpoint_matches_host_walk": True, "landed_bytes_match": True, "status": 0}
+
+
+def failed_checks(node, path="") -> list:
+    """Paths of every probe check in `node` (nested dicts) that failed."""
+    bad = []
+    if isinstance(node, dict):
+        for k, v in node.items():
+            p = f"{path}.{k}" if path else k
+            if k in CHECK_FLAGS and not isinstance(v, dict):
+                if v != CHECK_FLAGS[k]:
+                    bad.append(f"{p}={v}")
+            else:
+                bad += failed_checks(v, p)
+    return bad
+
+
 def run_ours(args) -> int:
     import torch
 
@@ -290,10 +309,16 @@ def run_ours(args) -> int:
     torch.cuda.empty_cache()
     if not args.no_probes:
         result["probes"] = run_probes(args, ranks, peaks)
+    # every rank's probe checks decide the exit code, so a wrong receive or
+    # result on any GPU fails the run instead of only flagging it
+    bad = failed_checks(result.get("probes", {}))
+    any_bad = ranks.sum(float(len(bad))) > 0
     if ranks.rank == 0:
         print(json.dumps(result), flush=True)
+    if bad:
+        print(f"rank {ranks.rank}: failed checks: {', '.join(bad)}", file=sys.stderr, flush=True)
     ranks.close()
-    return 0
+    return 1 if any_bad else 0
 
 
 def run_e2e(args, ranks, torch, dev_a, dev_b, nbytes):
@@ -463,12 +488,17 @@ def probe_tma(torch, stream, sh, peaks):
     out["load_only_4stage"] = {"GB/s": round(gbs, 2), "GiB/s": round(gbs / 1.073741824, 2),
                                "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
                                "status": int(status.item())}
-    buf = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    buf = torch.empty(1024, dtype=torch.uint8, device="cuda")
+    check("cmb_fill_bytes", ctypes.c_void_p(buf.data_ptr()), 1024, ctypes.c_uint64(SEED), sh)
     cyc = torch.zeros(1, dtype=torch.int32, device="cuda")
-    check("cmb_tma_1d_latency", ctypes.c_void_p(buf.data_ptr()), 1024, 256,
-          ctypes.c_void_p(cyc.data_ptr()), ctypes.c_void_p(status.data_ptr()), sh)
+    landed = torch.zeros(16, dtype=torch.uint8, device="cuda")
+    check("cmb_tma_1d_latency", ctypes.c_void_p(buf.data_ptr()), 1024, 0, 256,
+          ctypes.c_void_p(cyc.data_ptr()), ctypes.c_void_p(landed.data_ptr()),
+          ctypes.c_void_p(status.data_ptr()), sh)
     torch.cuda.synchronize()
-    out["tma_1d_load_latency_cyc"] = int(cyc.item()) / 256
+    out["tma_1d"] = {"load_latency_cyc": int(cyc.item()) / 256, "round_trips": 256,
+                     "landed_bytes_match": bool(torch.equal(landed, buf[:16])),
+                     "status": int(status.item())}
     del src, dst
     return out
 
@@ -477,8 +507,10 @@ def probe_gemm(torch, stream, sh, peaks):
     """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5, fp32 accumulation in
     TMEM, 2-CTA tiles of 256 x 512 (two N=256 accumulators per pair, held
     8-warp epilogue), and the 1-CTA 128x256 form; FP8 e4m3 with a per-tensor
-    scale.  TFLOP/s = 2*M*N*K / median launch time; 8 sampled 64x64 output
-    tiles are checked against an fp64 product.  cuBLAS (torch.mm /
+    scale.  TFLOP/s = 2*M*N*K / median launch time; every variant's output
+    is checked on 64 sampled 256x256 tiles (the two corner tiles included)
+    against an fp64 product of the same operands (max-norm per tile, rel
+    tol 1e-2).  cuBLAS (torch.mm /
     torch._scaled_mm) on the same operands with the same fp32 output is
     timed alongside as a live reference point; it is not part of the
     product."""
@@ -503,17 +535,24 @@ def probe_gemm(torch, stream, sh, peaks):
     check("cmb_quantize_e4m3", ctypes.c_void_p(B.data_ptr()), N * K, ctypes.c_void_p(qb.data_ptr()),
           ctypes.c_void_p(sb.data_ptr()), sh)
     g = torch.Generator().manual_seed(3)
-    rows = torch.randint(0, M // 64, (8,), generator=g) * 64
-    cols = torch.randint(0, N // 64, (8,), generator=g) * 64
+    T = 256  # sampled tile edge
+    rows = (torch.randint(0, M // T, (64,), generator=g) * T).tolist()
+    cols = (torch.randint(0, N // T, (64,), generator=g) * T).tolist()
+    rows[0], cols[0], rows[1], cols[1] = 0, 0, M - T, N - T
 
-    def sampled_err(a_f64, b_f64):
-        Cm = C.view(M, N)
+    def tiles_err(out, a_f64, b_f64):
+        """Max over the sampled tiles of max|C - C_fp64| / max|C_fp64|."""
+        Cm = out.view(M, N)
         worst = 0.0
-        for r, c in zip(rows.tolist(), cols.tolist()):
-            ref = a_f64[r:r + 64] @ b_f64[c:c + 64].T
-            got = Cm[r:r + 64, c:c + 64].double()
+        for r, c in zip(rows, cols):
+            ref = a_f64[r:r + T] @ b_f64[c:c + T].T
+            got = Cm[r:r + T, c:c + T].double()
+            if not bool(torch.isfinite(got).all()):
+                return float("inf")
             worst = max(worst, float((got - ref).abs().max() / ref.abs().max()))
         return worst
+
+    sampled_err = lambda a_f64, b_f64: tiles_err(C, a_f64, b_f64)
 
     a64 = A.view(M, K).view(torch.bfloat16).double()
     b64 = B.view(N, K).view(torch.bfloat16).double()
@@ -564,14 +603,7 @@ def probe_gemm(torch, stream, sh, peaks):
     a64 = A.view(M, K).view(torch.bfloat16).double()
     b64 = B.view(N, K).view(torch.bfloat16).double()
 
-    def sampled_err_b(a_f64, b_f64):
-        Cm = Cb.view(M, N)
-        worst = 0.0
-        for r, c in zip(rows.tolist(), cols.tolist()):
-            ref = a_f64[r:r + 64] @ b_f64[c:c + 64].T
-            got = Cm[r:r + 64, c:c + 64].double()
-            worst = max(worst, float((got - ref).abs().max() / ref.abs().max()))
-        return worst
+    sampled_err_b = lambda a_f64, b_f64: tiles_err(Cb, a_f64, b_f64)
 
     for label, fp8, ops, scales, (fa, fb) in (
             ("bf16_8192_2cta_bf16out", 0, (A, B), (None, None), (a64, b64)),
@@ -627,11 +659,62 @@ def probe_gemm(torch, stream, sh, peaks):
     return out
 
 
+def _nccl_reference(ranks, nbytes, reps=5, warm=2) -> dict:
+    """NCCL over the same links as a live reference point (not the product):
+    a ring of send/recv (rank r -> r+1) and all_to_all_single of `nbytes` per
+    GPU; per-GPU egress GB/s from the max-over-ranks median time."""
+    import torch
+
+    dist = ranks.dist
+    stream = torch.cuda.current_stream()
+    send = torch.empty(nbytes, dtype=torch.uint8, device="cuda").fill_(ranks.rank & 0xFF)
+    recv = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    nxt, prv = (ranks.rank + 1) % ranks.world, (ranks.rank - 1) % ranks.world
+
+    def ring():
+        ops = [dist.P2POp(dist.isend, send, nxt), dist.P2POp(dist.irecv, recv, prv)]
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+
+    def a2a():
+        dist.all_to_all_single(recv, send)
+
+    out = {}
+    for name, fn, egress in (("ring_nccl", ring, nbytes),
+                             ("alltoall_nccl", a2a, nbytes * (ranks.world - 1) // ranks.world)):
+        times = []
+        for rep in range(warm + reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            ranks.barrier()
+            torch.cuda.synchronize()
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            t = ranks.max(a.elapsed_time(b))
+            if rep >= warm:
+                times.append(t)
+        ms = statistics.median(times)
+        link = egress / (ms * 1e-3) / 1e9
+        ok = bool(torch.all(recv[:4096] == (prv if name == "ring_nccl" else 0) & 0xFF))
+        out[name] = {"per_gpu_egress_GB/s": round(link, 2), "frac_of_900_spec": round(link / 900.0, 4),
+                     "ms": round(ms, 4), "egress_bytes_per_gpu": egress,
+                     "received_first_chunk_ok": ok}
+    del send, recv
+    return out
+
+
 def probe_p2p(args, ranks) -> dict:
     """Config: 256 MiB seeded random bytes per GPU exchanged over NVLink,
-    ring (-> rank+1) and all-to-all (N chunks), by in-kernel peer stores, by
-    in-kernel bulk copies and by the copy engines; bit-exact receive check.  Time = max over ranks of
-    each rank's device time (CUDA events), median of 5 repetitions."""
+    ring (-> rank+1) and all-to-all (N chunks, each rank visiting its peers
+    in staggered order), by in-kernel peer stores, by in-kernel bulk copies
+    and by the copy engines (all peers at once, or one or two streams
+    visiting them in turn); bit-exact receive check.  Time = max over ranks
+    of each rank's device time (CUDA events), median of 5 repetitions.  The
+    fraction of the peer-copy ceiling divides by the copy engines' ring rate
+    measured in the same run; NCCL's send/recv ring and all_to_all_single on
+    the same sizes are timed alongside as a reference point."""
     import torch
 
     from cuda_micro_bench_b200 import multi_gpu
@@ -641,10 +724,13 @@ def probe_p2p(args, ranks) -> dict:
     sh = ctypes.c_void_p(stream.cuda_stream)
     ex = multi_gpu.PeerExchange(ranks, nbytes, SEED)
     out = {}
+    methods = {"ring": ("copy_engine", "store", "bulk"),
+               "alltoall": ("store", "bulk", "copy_engine", "copy_engine_1stream",
+                            "copy_engine_2stream")}
     try:
         for mode in ("ring", "alltoall"):
             egress = multi_gpu.egress_bytes(mode, ranks.rank, ranks.world, nbytes)
-            for method in ("store", "bulk", "copy_engine"):
+            for method in methods[mode]:
                 times = []
                 for rep in range(2 + 5):
                     a = torch.cuda.Event(enable_timing=True)
@@ -666,13 +752,22 @@ def probe_p2p(args, ranks) -> dict:
                     "per_gpu_egress_GB/s": round(link, 2),
                     "aggregate_GB/s": round(ranks.world * link, 2),
                     "frac_of_900_spec": round(link / 900.0, 4),
-                    "frac_of_770_measured_peer_copy": round(link / 770.0, 4),
                     "ms": round(ms, 4), "egress_bytes_per_gpu": egress,
-                    "sm_ctas": {"store": "2 per SM", "bulk": "32 per job (<= SMs / jobs)",
-                                "copy_engine": "0 (copy engines)"}[method],
+                    "sm_ctas": {"store": "2 per SM", "bulk": "32 per job (<= SMs / jobs)"}.get(
+                        method, "0 (copy engines)"),
                     "bit_exact": bad == 0}
+        ceiling = out["ring_copy_engine"]["per_gpu_egress_GB/s"]
+        for v in out.values():
+            v["frac_of_measured_peer_copy"] = round(v["per_gpu_egress_GB/s"] / ceiling, 4)
+        out["measured_peer_copy_GB/s"] = {
+            "value": ceiling, "what": "copy engines, 256 MiB ring, this run (the denominator of "
+                                      "frac_of_measured_peer_copy)"}
     finally:
         ex.close()
+    try:
+        out["nccl_reference"] = _nccl_reference(ranks, nbytes)
+    except (RuntimeError, AttributeError) as e:  # reference point only
+        out["nccl_reference"] = {"error": str(e).splitlines()[0][:200]}
     return out
 
 

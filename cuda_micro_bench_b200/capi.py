@@ -26,6 +26,7 @@ SIGNATURES = {
     "cmb_status_string": (_s, [_i]),
     "cmb_last_error": (_s, []),
     "cmb_version": (_s, []),
+    "cmb_device_reset": (_i, []),
     "cmb_fill_hash_u32": (_i, [_p, _sz, _p]),
     "cmb_fill_uniform_f32": (_i, [_p, _sz, _u64, _p]),
     "cmb_fill_bytes": (_i, [_p, _sz, _u64, _p]),
@@ -44,7 +45,7 @@ SIGNATURES = {
     "cmb_tma_tile_copy_bf16": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
     "cmb_tma_tile_copy_tuned": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _p]),
     "cmb_tma_tile_load_bf16": (_i, [_p, _i, _i, _i, _i, _i, _p, _sz, _p, _p]),
-    "cmb_tma_1d_latency": (_i, [_p, _sz, _i, _p, _p, _p]),
+    "cmb_tma_1d_latency": (_i, [_p, _sz, _sz, _i, _p, _p, _p, _p]),
     "cmb_gemm_bf16": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "cmb_gemm_e4m3": (_i, [_p, _p, _p, _i, _i, _i, _p, _p, _i, _p, _p]),
     "cmb_gemm_tuned": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
@@ -65,6 +66,7 @@ SIGNATURES = {
     "cmb_p2p_scatter_bulk": (_i, [_p, _p, _p, _i, _i, _p, _p]),
     "cmb_p2p_scatter_bulk_tuned": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "cmb_p2p_scatter_copy_engine": (_i, [_p, _p, _p, _i, _p]),
+    "cmb_p2p_scatter_copy_engine_tuned": (_i, [_p, _p, _p, _i, _i, _p]),
     "cmb_selftest_wait_timeout": (_i, [_u64, _p, _p, _p]),
     "cmb_compare_bytes": (_i, [_p, _p, _sz, _p, _p]),
     "cmb_benchmark_global_memory": (_i, []),
@@ -73,6 +75,8 @@ SIGNATURES = {
     "cmb_benchmark_tensor_core": (_i, []),
     "cmb_benchmark_tensor_core_extended": (_i, []),
     "cmb_benchmark_multi_gpu": (_i, []),
+    "cmb_benchmark_memory_more": (_i, []),
+    "cmb_benchmark_pcie": (_i, []),
     "cmb_results_log_report_placeholders": (_i, []),
     "cmb_report_key_count": (ctypes.c_size_t, []),
     "cmb_report_key": (_i, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_char_p),
@@ -82,6 +86,7 @@ SIGNATURES = {
     "cmb_results_log": (_i, [_s, _s, _d, _s]),
     "cmb_results_write_json": (_i, [_s]),
     "cmb_results_clear": (_i, []),
+    "cmb_results_set_sink": (_i, [_p, _p, _p]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

@@ -60,6 +60,9 @@ __global__ void k_chase(const uint32_t *links, uint64_t warmup, uint64_t hops, u
 uint64_t splitmix_at(uint64_t seed, uint64_t i) { return dev::splitmix64_at(seed, i); }
 
 }  // namespace
+
+uint64_t splitmix64_host(uint64_t seed, uint64_t i) { return dev::splitmix64_at(seed, i); }
+
 }  // namespace cmb
 
 using namespace cmb;

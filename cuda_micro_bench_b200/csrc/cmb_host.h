@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstddef>
+#include <cstdint>
 
 #include "../../include/cmb_b200.h"
 
@@ -19,6 +20,15 @@ void clear_error();
 int current_sm_count();
 // Compute capability major*10+minor of the current device.
 int current_cc();
+
+// Output i of the SplitMix64 stream of `seed`, on the host (the generator
+// of the cmb_fill_* kernels).
+uint64_t splitmix64_host(uint64_t seed, uint64_t i);
+
+// Release the library's cached streams and events of device `dev`
+// (cmb_device_reset calls these before resetting the device).
+void p2p_release_streams(int dev);
+void host_copy_release_streams(int dev);
 
 // The source file's name without its directories (error messages name the
 // file, not the machine it was built on).

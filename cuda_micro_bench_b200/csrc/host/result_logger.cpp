@@ -21,12 +21,23 @@ void ResultLogger::setDevice(const std::string &name, const std::string &arch, i
   clock_khz_ = clock_khz;
   mem_clock_khz_ = mem_clock_khz;
   mem_bus_width_ = mem_bus_width;
+  if (sink_device_ != nullptr)
+    sink_device_(name.c_str(), arch.c_str(), sm_count, clock_khz, mem_clock_khz, mem_bus_width,
+                 sink_user_);
 }
 
 void ResultLogger::log(const std::string &section, const std::string &key, double value,
                        const std::string &unit) {
   std::lock_guard<std::mutex> lock(mu_);
   sections_[section][key] = Entry{value, unit};
+  if (sink_log_ != nullptr) sink_log_(section.c_str(), key.c_str(), value, unit.c_str(), sink_user_);
+}
+
+void ResultLogger::setSink(cmb_results_log_fn log, cmb_results_device_fn device, void *user) {
+  std::lock_guard<std::mutex> lock(mu_);
+  sink_log_ = log;
+  sink_device_ = device;
+  sink_user_ = user;
 }
 
 bool ResultLogger::hasDevice() const {
@@ -142,5 +153,11 @@ extern "C" int cmb_results_write_json(const char *path) {
 
 extern "C" int cmb_results_clear(void) {
   g_results.clear();
+  return CMB_OK;
+}
+
+extern "C" int cmb_results_set_sink(cmb_results_log_fn log, cmb_results_device_fn device,
+                                    void *user) {
+  cmb::g_results.setSink(log, device, user);
   return CMB_OK;
 }

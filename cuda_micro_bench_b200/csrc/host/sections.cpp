@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -190,39 +191,72 @@ float e4m3_to_float(uint8_t v) {
   return static_cast<float>(x);
 }
 
-// Max over `tiles` sampled 64x64 tiles of max|C - C_fp64| / max|C_fp64|.
+// Runs fn(i) for i in [0, n) on all host threads.
+template <class F>
+void parallel_for(int n, F fn) {
+  const int t = std::max(1, std::min<int>(n, static_cast<int>(std::thread::hardware_concurrency())));
+  std::vector<std::thread> pool;
+  std::atomic<int> next{0};
+  for (int k = 0; k < t; ++k)
+    pool.emplace_back([&] {
+      for (int i = next++; i < n; i = next++) fn(i);
+    });
+  for (auto &th : pool) th.join();
+}
+
+// Max over `tiles` sampled T x T output tiles (the first and the last
+// corner tile, then tiles drawn from a fixed LCG) of
+// max|C - C_fp64| / max|C_fp64| within the tile: the max-norm reading of
+// the stated "rel tol 1e-2".  Each fp64 product is summed in k order; the
+// tile's B columns are decoded once (k-major) and the row blocks are spread
+// over the host's threads.
 template <bool kFp8>
 double sampled_gemm_error(const std::vector<uint8_t> &A, const std::vector<uint8_t> &B,
                           const std::vector<float> &C, int M, int N, int K, double sa, double sb,
                           int tiles) {
+  constexpr int T = 256, RB = 4, CB = 16;
+  auto elem = [&](const std::vector<uint8_t> &X, size_t i, double s) -> double {
+    if (kFp8) return e4m3_to_float(X[i]) * s;
+    uint16_t v;
+    std::memcpy(&v, &X[2 * i], 2);
+    return bf16_bits_to_float(v);
+  };
   double worst = 0.0;
   uint64_t r = 12345;
-  std::vector<double> a(64 * (size_t)K), b(64 * (size_t)K);
+  std::vector<double> bt((size_t)K * T), ref((size_t)T * T);
   for (int t = 0; t < tiles; ++t) {
     r = r * 6364136223846793005ull + 1442695040888963407ull;
-    const int r0 = static_cast<int>((r >> 33) % (M / 64)) * 64;
-    const int c0 = static_cast<int>((r >> 13) % (N / 64)) * 64;
-    for (int i = 0; i < 64; ++i)
-      for (int k = 0; k < K; ++k) {
-        const size_t ia = (size_t)(r0 + i) * K + k, ib = (size_t)(c0 + i) * K + k;
-        if (kFp8) {
-          a[(size_t)i * K + k] = e4m3_to_float(A[ia]) * sa;
-          b[(size_t)i * K + k] = e4m3_to_float(B[ib]) * sb;
-        } else {
-          uint16_t va, vb;
-          std::memcpy(&va, &A[2 * ia], 2);
-          std::memcpy(&vb, &B[2 * ib], 2);
-          a[(size_t)i * K + k] = bf16_bits_to_float(va);
-          b[(size_t)i * K + k] = bf16_bits_to_float(vb);
+    int r0 = static_cast<int>((r >> 33) % (M / T)) * T;
+    int c0 = static_cast<int>((r >> 13) % (N / T)) * T;
+    if (t == 0) r0 = c0 = 0;
+    if (t == 1) r0 = M - T, c0 = N - T;
+    parallel_for(K, [&](int k) {
+      for (int j = 0; j < T; ++j) bt[(size_t)k * T + j] = elem(B, (size_t)(c0 + j) * K + k, sb);
+    });
+    parallel_for(T / RB, [&](int blk) {
+      std::vector<double> a((size_t)RB * K);
+      for (int q = 0; q < RB; ++q)
+        for (int k = 0; k < K; ++k) a[(size_t)q * K + k] = elem(A, (size_t)(r0 + blk * RB + q) * K + k, sa);
+      for (int j0 = 0; j0 < T; j0 += CB) {
+        double acc[RB][CB] = {};
+        for (int k = 0; k < K; ++k) {
+          const double *b = &bt[(size_t)k * T + j0];
+          for (int q = 0; q < RB; ++q) {
+            const double aq = a[(size_t)q * K + k];
+            for (int j = 0; j < CB; ++j) acc[q][j] += aq * b[j];
+          }
         }
+        for (int q = 0; q < RB; ++q)
+          for (int j = 0; j < CB; ++j) ref[(size_t)(blk * RB + q) * T + j0 + j] = acc[q][j];
       }
+    });
     double ref_max = 0.0, err_max = 0.0;
-    for (int i = 0; i < 64; ++i)
-      for (int j = 0; j < 64; ++j) {
-        double s = 0.0;
-        for (int k = 0; k < K; ++k) s += a[(size_t)i * K + k] * b[(size_t)j * K + k];
+    for (int i = 0; i < T; ++i)
+      for (int j = 0; j < T; ++j) {
+        const double s = ref[(size_t)i * T + j];
+        const double c = C[(size_t)(r0 + i) * N + c0 + j];
         ref_max = std::max(ref_max, std::fabs(s));
-        err_max = std::max(err_max, std::fabs(C[(size_t)(r0 + i) * N + c0 + j] - s));
+        err_max = std::max(err_max, std::isfinite(c) ? std::fabs(c - s) : HUGE_VAL);
       }
     worst = std::max(worst, err_max / std::max(ref_max, 1e-300));
   }
@@ -255,7 +289,7 @@ int query_device(int dev, DeviceInfo *info) {
 }
 
 // --device: the device header and derived peaks (src/device_info.cu:6-59).
-int benchmark_device_info() {
+int section_device_info() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Device Info ===\n  %s, cc %d.%d, %d SMs, %.2f GiB, L2 %d KiB, clock %.3f GHz\n",
@@ -277,7 +311,7 @@ int benchmark_device_info() {
   return CMB_OK;
 }
 
-int benchmark_global_memory() {
+int section_global_memory() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Global Memory Benchmarks (median of 5) ===\n");
@@ -346,7 +380,7 @@ int benchmark_global_memory() {
   return CMB_OK;
 }
 
-int benchmark_cache() {
+int section_cache() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Cache Benchmarks (random dependent loads, median of 5) ===\n");
@@ -373,7 +407,7 @@ int benchmark_cache() {
 // --memory-more: L2 aggregate read bandwidth (src/memory_more.cu:201-234):
 // an L2-resident buffer of min(8 MiB, L2/4) read 1024 times by 4 CTAs per
 // SM; median of five after one warm-up; the exact word sum is checked.
-int benchmark_memory_more() {
+int section_memory_more() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Memory (L2 aggregate bandwidth) ===\n");
@@ -408,44 +442,83 @@ int benchmark_memory_more() {
 
 // --pcie: pinned host <-> device copy bandwidth (src/pcie.cu:55-97): 64 MiB,
 // ten copies per direction after a warm-up, device-timed.
-int benchmark_pcie() {
+// Pinned host buffer owned by a section.
+struct PinnedBuf {
+  void *p = nullptr;
+  PinnedBuf() = default;
+  PinnedBuf(const PinnedBuf &) = delete;
+  ~PinnedBuf() {
+    if (p != nullptr) cudaFreeHost(p);
+  }
+  int alloc(size_t bytes) {
+    CMB_CUDA_TRY(cudaMallocHost(&p, bytes));
+    return CMB_OK;
+  }
+};
+
+// bytes of the cmb_fill_bytes stream of `seed`, generated on the host.
+void host_seeded_bytes(uint8_t *dst, size_t bytes, uint64_t seed) {
+  size_t i = 0;
+  for (; i + 8 <= bytes; i += 8) {
+    const uint64_t w = splitmix64_host(seed, i / 8);
+    std::memcpy(dst + i, &w, 8);
+  }
+  for (; i < bytes; ++i) dst[i] = static_cast<uint8_t>(splitmix64_host(seed, i / 8) >> (8 * (i & 7)));
+}
+
+int section_pcie() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== PCIe (pinned host <-> device) ===\n");
+  // 64 MiB pinned buffer, 10 copies per timing (src/pcie.cu:55-97).  The
+  // host-to-device copies carry seeded bytes, checked on the device against
+  // the same stream generated there; the device-to-host copies carry another
+  // seed's bytes, checked on the host.
   const size_t bytes = 64ull << 20;
-  void *host = nullptr;
-  CMB_CUDA_TRY(cudaMallocHost(&host, bytes));
-  DevBuf dev;
-  int rc = dev.alloc(bytes);
+  constexpr uint64_t kUpSeed = 0x9C1E, kDownSeed = 0x9C1F;
+  PinnedBuf host;
+  TRY(host.alloc(bytes));
+  DevBuf dev, ref, count;
+  TRY(dev.alloc(bytes));
+  TRY(ref.alloc(bytes));
+  TRY(count.alloc(sizeof(unsigned long long)));
+  host_seeded_bytes(static_cast<uint8_t *>(host.p), bytes, kUpSeed);
   double h2d = 0, d2h = 0;
-  if (rc == CMB_OK) {
-    std::memset(host, 0x5a, bytes);
-    rc = time_median(
-        [&]() -> int {
-          for (int r = 0; r < 10; ++r)
-            CMB_CUDA_TRY(cudaMemcpyAsync(dev.p, host, bytes, cudaMemcpyHostToDevice, nullptr));
-          return CMB_OK;
-        },
-        2, 1, &h2d);
-  }
-  if (rc == CMB_OK)
-    rc = time_median(
-        [&]() -> int {
-          for (int r = 0; r < 10; ++r)
-            CMB_CUDA_TRY(cudaMemcpyAsync(host, dev.p, bytes, cudaMemcpyDeviceToHost, nullptr));
-          return CMB_OK;
-        },
-        2, 1, &d2h);
-  cudaFreeHost(host);
-  if (rc != CMB_OK) return rc;
+  TRY(time_median(
+      [&]() -> int {
+        for (int r = 0; r < 10; ++r)
+          CMB_CUDA_TRY(cudaMemcpyAsync(dev.p, host.p, bytes, cudaMemcpyHostToDevice, nullptr));
+        return CMB_OK;
+      },
+      2, 1, &h2d));
+  TRY(cmb_fill_bytes(ref.as<uint8_t>(), bytes, kUpSeed, nullptr));
+  TRY(cmb_compare_bytes(dev.p, ref.p, bytes, count.as<unsigned long long>(), nullptr));
+  unsigned long long up_bad = 0;
+  CMB_CUDA_TRY(cudaMemcpy(&up_bad, count.p, sizeof(up_bad), cudaMemcpyDeviceToHost));
+  TRY(cmb_fill_bytes(dev.as<uint8_t>(), bytes, kDownSeed, nullptr));
+  TRY(time_median(
+      [&]() -> int {
+        for (int r = 0; r < 10; ++r)
+          CMB_CUDA_TRY(cudaMemcpyAsync(host.p, dev.p, bytes, cudaMemcpyDeviceToHost, nullptr));
+        return CMB_OK;
+      },
+      2, 1, &d2h));
+  std::vector<uint8_t> want(bytes);
+  host_seeded_bytes(want.data(), bytes, kDownSeed);
+  const bool down_ok = std::memcmp(want.data(), host.p, bytes) == 0;
   const double up = gib_per_s(10.0 * bytes, h2d), down = gib_per_s(10.0 * bytes, d2h);
-  printf("  HtoD pinned bandwidth: %.2f GiB/s\n  DtoH pinned bandwidth: %.2f GiB/s\n", up, down);
+  printf("  HtoD pinned bandwidth: %.2f GiB/s (%s)\n  DtoH pinned bandwidth: %.2f GiB/s (%s)\n",
+         up, up_bad == 0 ? "bytes verified" : "MISMATCH", down, down_ok ? "bytes verified" : "MISMATCH");
+  if (up_bad != 0)
+    return fail(CMB_ERR_MISMATCH, "PCIe: %llu words differ after the host-to-device copies", up_bad);
+  if (!down_ok) return fail(CMB_ERR_MISMATCH, "PCIe: the device-to-host copies differ");
   g_results.log("pcie", "htod_bandwidth_GiB_s", up, "GiB/s");
   g_results.log("pcie", "dtoh_bandwidth_GiB_s", down, "GiB/s");
+  g_results.log("pcie", "verified", 1.0, "bool");
   return CMB_OK;
 }
 
-int benchmark_tma() {
+int section_tma() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== TMA (cp.async.bulk.tensor) Probes ===\n");
@@ -456,20 +529,31 @@ int benchmark_tma() {
     return fail(CMB_ERR_UNSUPPORTED, "TMA probes need an sm_100 device");
   }
   {
-    DevBuf buf, cyc, st;
+    // 1 KiB of hashed words; the reference's 16-byte load from coordinate
+    // 0, 256 times, and the bytes it left in shared memory checked.
+    DevBuf buf, cyc, st, landed;
     TRY(buf.alloc(1024));
     TRY(cyc.alloc(sizeof(uint32_t)));
     TRY(st.alloc(sizeof(int)));
-    CMB_CUDA_TRY(cudaMemset(buf.p, 0, 1024));
+    TRY(landed.alloc(16));
+    TRY(cmb_fill_hash_u32(buf.as<uint32_t>(), 256, nullptr));
     const int iters = 256;
-    TRY(cmb_tma_1d_latency(buf.p, 1024, iters, cyc.as<uint32_t>(), st.as<int>(), nullptr));
+    TRY(cmb_tma_1d_latency(buf.p, 1024, 0, iters, cyc.as<uint32_t>(), landed.as<uint8_t>(),
+                           st.as<int>(), nullptr));
     uint32_t h = 0;
     int status = 0;
+    uint8_t got[16], want[16];
     CMB_CUDA_TRY(cudaMemcpy(&h, cyc.p, sizeof(h), cudaMemcpyDeviceToHost));
     CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+    CMB_CUDA_TRY(cudaMemcpy(got, landed.p, 16, cudaMemcpyDeviceToHost));
+    CMB_CUDA_TRY(cudaMemcpy(want, buf.p, 16, cudaMemcpyDeviceToHost));
     if (status != 0) return fail(status, "TMA 1-D latency: a bounded wait expired");
-    printf("  TMA 1D 16-byte load issue/wait cost: %.2f cycles\n", (double)h / iters);
+    if (std::memcmp(got, want, 16) != 0)
+      return fail(CMB_ERR_MISMATCH, "TMA 1-D latency: the landed bytes differ from the source");
+    printf("  TMA 1D 16-byte load issue/wait cost: %.2f cycles (landed bytes verified)\n",
+           (double)h / iters);
     g_results.log("tma", "tma_1d_load_latency_cyc", (double)h / iters, "cycles");
+    g_results.log("tma", "tma_1d_verified", 1.0, "bool");
   }
   // 16384 x 16384 bf16, 128 x 128 boxes, 4-stage ring.
   const int n = 16384;
@@ -557,7 +641,7 @@ int mma_sync_probe(const DeviceInfo &info, int kind, const char *section, const 
 
 }  // namespace
 
-int benchmark_tensor_core() {
+int section_tensor_core() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Tensor Core Benchmarks ===\n");
@@ -588,7 +672,7 @@ int benchmark_tensor_core() {
   return CMB_OK;
 }
 
-int benchmark_tensor_core_extended() {
+int section_tensor_core_extended() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Tensor Core Extended ===\n");
@@ -641,8 +725,9 @@ int benchmark_tensor_core_extended() {
       CMB_CUDA_TRY(cudaMemcpy(hs, sa.p, sizeof(hs), cudaMemcpyDeviceToHost));
       CMB_CUDA_TRY(cudaMemcpy(hs2, sb.p, sizeof(hs2), cudaMemcpyDeviceToHost));
     }
-    const double err = fp8 ? sampled_gemm_error<true>(ha, hb, hc, M, N, K, hs[0], hs2[0], 8)
-                           : sampled_gemm_error<false>(ha, hb, hc, M, N, K, 1.0, 1.0, 8);
+    // 64 sampled 256 x 256 output tiles against fp64 products
+    const double err = fp8 ? sampled_gemm_error<true>(ha, hb, hc, M, N, K, hs[0], hs2[0], 64)
+                           : sampled_gemm_error<false>(ha, hb, hc, M, N, K, 1.0, 1.0, 64);
     const double tf = flop / (ms * 1e-3) / 1e12;
     const double spec = fp8 ? 4500.0 : 2250.0;
     const std::string p = fp8 ? "fp8_e4m3_gemm_8192" : "bf16_gemm_8192";
@@ -736,11 +821,14 @@ int p2p_step(std::vector<GpuSide> &g, size_t bytes, bool alltoall, P2PMethod met
       nb[0] = bytes;
       jobs = 1;
     } else {
+      // Staggered: GPU d visits peers d+1, d+2, ... and its own chunk last,
+      // so at each position of the job list every GPU has one sender.
       const size_t c = bytes / n;
-      for (int j = 0; j < n; ++j) {
-        dst[j] = static_cast<char *>(g[j].recv) + (size_t)s.dev * c;
-        src[j] = static_cast<const char *>(s.send) + (size_t)j * c;
-        nb[j] = c;
+      for (int k = 0; k < n; ++k) {
+        const int j = (s.dev + 1 + k) % n;
+        dst[k] = static_cast<char *>(g[j].recv) + (size_t)s.dev * c;
+        src[k] = static_cast<const char *>(s.send) + (size_t)j * c;
+        nb[k] = c;
       }
       jobs = n;
     }
@@ -870,7 +958,7 @@ int multi_gpu_body(std::vector<GpuSide> &g, size_t bytes) {
 
 }  // namespace
 
-int benchmark_multi_gpu() {
+int section_multi_gpu() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   int count = 0;
@@ -923,15 +1011,15 @@ struct Section {
 };
 
 const Section kSections[] = {
-    {"--device", "Device / SM info and derived peaks", benchmark_device_info},
-    {"--memory", "HBM read/copy streams and DRAM pointer chase", benchmark_global_memory},
-    {"--cache", "L1/L2 dependent-load latency sweep", benchmark_cache},
-    {"--memory-more", "L2 aggregate read bandwidth", benchmark_memory_more},
-    {"--pcie", "Pinned host <-> device copy bandwidth", benchmark_pcie},
-    {"--tma", "TMA bulk-tensor latency, tile load and tile copy", benchmark_tma},
-    {"--tensor", "mma.sync TF32 and tcgen05 issue-rate probes", benchmark_tensor_core},
-    {"--tensor-ext", "mma.sync FP16/BF16/FP8/INT8 and tcgen05 BF16/FP8 GEMM", benchmark_tensor_core_extended},
-    {"--p2p", "Multi-GPU sharded stream and NVLink peer copies", benchmark_multi_gpu},
+    {"--device", "Device / SM info and derived peaks", section_device_info},
+    {"--memory", "HBM read/copy streams and DRAM pointer chase", section_global_memory},
+    {"--cache", "L1/L2 dependent-load latency sweep", section_cache},
+    {"--memory-more", "L2 aggregate read bandwidth", section_memory_more},
+    {"--pcie", "Pinned host <-> device copy bandwidth", section_pcie},
+    {"--tma", "TMA bulk-tensor latency, tile load and tile copy", section_tma},
+    {"--tensor", "mma.sync TF32 and tcgen05 issue-rate probes", section_tensor_core},
+    {"--tensor-ext", "mma.sync FP16/BF16/FP8/INT8 and tcgen05 BF16/FP8 GEMM", section_tensor_core_extended},
+    {"--p2p", "Multi-GPU sharded stream and NVLink peer copies", section_multi_gpu},
 };
 
 void usage(const char *name) {
@@ -1016,12 +1104,14 @@ int run_cli(int argc, const char *const *argv, const char *json_path) {
 
 using namespace cmb;
 
-extern "C" int cmb_benchmark_global_memory(void) { return benchmark_global_memory(); }
-extern "C" int cmb_benchmark_cache(void) { return benchmark_cache(); }
-extern "C" int cmb_benchmark_tma(void) { return benchmark_tma(); }
-extern "C" int cmb_benchmark_tensor_core(void) { return benchmark_tensor_core(); }
-extern "C" int cmb_benchmark_tensor_core_extended(void) { return benchmark_tensor_core_extended(); }
-extern "C" int cmb_benchmark_multi_gpu(void) { return benchmark_multi_gpu(); }
+extern "C" int cmb_benchmark_global_memory(void) { return section_global_memory(); }
+extern "C" int cmb_benchmark_cache(void) { return section_cache(); }
+extern "C" int cmb_benchmark_tma(void) { return section_tma(); }
+extern "C" int cmb_benchmark_tensor_core(void) { return section_tensor_core(); }
+extern "C" int cmb_benchmark_tensor_core_extended(void) { return section_tensor_core_extended(); }
+extern "C" int cmb_benchmark_multi_gpu(void) { return section_multi_gpu(); }
+extern "C" int cmb_benchmark_memory_more(void) { return section_memory_more(); }
+extern "C" int cmb_benchmark_pcie(void) { return section_pcie(); }
 extern "C" int cmb_results_log_report_placeholders(void) {
   log_report_placeholders();
   return CMB_OK;

@@ -1,12 +1,14 @@
 // sections.h — the reference's probe sections on top of the C ABI.
 //
-// Same entry points and result keys as the reference's
-// `void cmb::benchmark_<section>()` (src/main.cu:9-32): each section
-// queries device 0, allocates its buffers, runs the B200 kernels through
-// include/cmb_b200.h, checks their outputs, times them with CUDA events and
-// logs into g_results.  Where the reference exits on a CUDA error
-// (include/utils.h:11-19) or a failed self-check (include/memory_chase.h:161-164),
-// these return a cmb_status; the CLI turns a failure into exit code 1.
+// Same result keys as the reference's `void cmb::benchmark_<section>()`
+// (src/main.cu:9-32): each section queries device 0, allocates its buffers,
+// runs the B200 kernels through include/cmb_b200.h, checks their outputs,
+// times them with CUDA events and logs into g_results.  The section_*
+// functions return a cmb_status where the reference exits on a CUDA error
+// (include/utils.h:11-19) or a failed self-check
+// (include/memory_chase.h:161-164); the CLI turns a failure into exit code 1.
+// reference_entry.cpp wraps them in the reference's own signatures and
+// error behaviour (void, exit on failure) for the reference's main.cu.
 #pragma once
 
 #include <string>
@@ -32,14 +34,15 @@ struct DeviceInfo {
 // results file's device header (include/utils.h:47-82).
 int query_device(int dev, DeviceInfo *info);
 
-int benchmark_global_memory();       // --memory      (src/mem_global.cu:27-75)
-int benchmark_cache();               // --cache       (src/mem_cache.cu:4-24)
-int benchmark_memory_more();         // --memory-more (src/memory_more.cu:201-234, L2 only)
-int benchmark_pcie();                // --pcie        (src/pcie.cu:55-97, bandwidth only)
-int benchmark_tma();                 // --tma         (src/tma.cu:157-259)
-int benchmark_tensor_core();         // --tensor      (src/tensor_core.cu:66-120)
-int benchmark_tensor_core_extended();  // --tensor-ext (src/tensor_core_extended.cu:321-357)
-int benchmark_multi_gpu();           // --p2p         (new: sharded stream + NVLink P2P)
+int section_device_info();         // --device      (src/device_info.cu, header keys only)
+int section_global_memory();       // --memory      (src/mem_global.cu:27-75)
+int section_cache();               // --cache       (src/mem_cache.cu:4-24)
+int section_memory_more();         // --memory-more (src/memory_more.cu:201-234, L2 only)
+int section_pcie();                // --pcie        (src/pcie.cu:55-97, bandwidth only)
+int section_tma();                 // --tma         (src/tma.cu:157-259)
+int section_tensor_core();         // --tensor      (src/tensor_core.cu:66-120)
+int section_tensor_core_extended();  // --tensor-ext (src/tensor_core_extended.cu:321-357)
+int section_multi_gpu();           // --p2p         (new: sharded stream + NVLink P2P)
 
 // Logs every results key the reference's report reads and no section
 // measured, as "N/A" (null), so the report renders.

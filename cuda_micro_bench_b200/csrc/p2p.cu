@@ -168,9 +168,12 @@ struct CeStreams {
   bool ok = false;
 };
 
+std::mutex g_ce_mu;
+CeStreams g_ce_per_dev[64];
+
 CeStreams *ce_streams_for_current_device() {
-  static std::mutex mu;
-  static CeStreams per_dev[64];
+  std::mutex &mu = g_ce_mu;
+  CeStreams *per_dev = g_ce_per_dev;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
@@ -199,6 +202,22 @@ int check_jobs(const char *fn, void *const *dst, const void *const *src, const s
 }
 
 }  // namespace
+
+// Destroys the copy-engine streams and events of device `dev` (before a
+// device reset, which would leave their handles dangling).
+void p2p_release_streams(int dev) {
+  if (dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lock(g_ce_mu);
+  CeStreams &c = g_ce_per_dev[dev];
+  if (!c.ok) return;
+  for (int i = 0; i < kMaxJobs; ++i) {
+    cudaStreamDestroy(c.s[i]);
+    cudaEventDestroy(c.join[i]);
+  }
+  cudaEventDestroy(c.fork);
+  c = CeStreams{};
+}
+
 }  // namespace cmb
 
 using namespace cmb;
@@ -377,21 +396,44 @@ extern "C" int cmb_p2p_scatter_bulk_tuned(void *const *dst, const void *const *s
   return scatter_bulk(dst, src, bytes, n, ctas_per_job, chunk_bytes, stages, status, stream);
 }
 
-extern "C" int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src,
-                                           const size_t *bytes, int n, cmb_stream_t stream) {
+namespace cmb {
+namespace {
+
+int scatter_copy_engine(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                        int streams, cmb_stream_t stream) {
   int rc = check_jobs("cmb_p2p_scatter_copy_engine", dst, src, bytes, n);
   if (rc) return rc;
+  if (streams < 1 || streams > kMaxJobs)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_copy_engine: %d streams not in [1, 8]",
+                streams);
   CeStreams *c = ce_streams_for_current_device();
   if (c == nullptr) return fail(CMB_ERR_CUDA, "copy-engine streams could not be created");
-  // fork the jobs onto one stream each, so every destination's copy engine
-  // work runs concurrently, then join them back into `stream`
+  // Fork onto `streams` internal streams, job j on stream j % streams in the
+  // given order (jobs that share a stream run one after another), then join
+  // them back into `stream`.
+  const int used = streams < n ? streams : n;
   CMB_CUDA_TRY(cudaEventRecord(c->fork, stream));
-  for (int j = 0; j < n; ++j) {
-    CMB_CUDA_TRY(cudaStreamWaitEvent(c->s[j], c->fork, 0));
+  for (int q = 0; q < used; ++q) CMB_CUDA_TRY(cudaStreamWaitEvent(c->s[q], c->fork, 0));
+  for (int j = 0; j < n; ++j)
     if (bytes[j] > 0)
-      CMB_CUDA_TRY(cudaMemcpyAsync(dst[j], src[j], bytes[j], cudaMemcpyDefault, c->s[j]));
-    CMB_CUDA_TRY(cudaEventRecord(c->join[j], c->s[j]));
-    CMB_CUDA_TRY(cudaStreamWaitEvent(stream, c->join[j], 0));
+      CMB_CUDA_TRY(cudaMemcpyAsync(dst[j], src[j], bytes[j], cudaMemcpyDefault, c->s[j % used]));
+  for (int q = 0; q < used; ++q) {
+    CMB_CUDA_TRY(cudaEventRecord(c->join[q], c->s[q]));
+    CMB_CUDA_TRY(cudaStreamWaitEvent(stream, c->join[q], 0));
   }
   return CMB_OK;
+}
+
+}  // namespace
+}  // namespace cmb
+
+extern "C" int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src,
+                                           const size_t *bytes, int n, cmb_stream_t stream) {
+  return scatter_copy_engine(dst, src, bytes, n, n, stream);
+}
+
+extern "C" int cmb_p2p_scatter_copy_engine_tuned(void *const *dst, const void *const *src,
+                                                 const size_t *bytes, int n, int streams,
+                                                 cmb_stream_t stream) {
+  return scatter_copy_engine(dst, src, bytes, n, streams, stream);
 }

@@ -62,3 +62,12 @@ extern "C" const char *cmb_status_string(int status) {
 extern "C" const char *cmb_last_error(void) { return cmb::t_last_error.c_str(); }
 
 extern "C" const char *cmb_version(void) { return "cmb_b200 0.1 (sm_100a)"; }
+
+extern "C" int cmb_device_reset(void) {
+  int dev = 0;
+  CMB_CUDA_TRY(cudaGetDevice(&dev));
+  cmb::p2p_release_streams(dev);
+  cmb::host_copy_release_streams(dev);
+  CMB_CUDA_TRY(cudaDeviceReset());
+  return CMB_OK;
+}

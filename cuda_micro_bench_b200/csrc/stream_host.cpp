@@ -18,9 +18,12 @@ struct HostCopyStreams {
   bool ok = false;
 };
 
+std::mutex g_copy_mu;
+HostCopyStreams g_copy_per_dev[64];
+
 HostCopyStreams *streams_for_current_device() {
-  static std::mutex mu;
-  static HostCopyStreams per_dev[64];
+  std::mutex &mu = g_copy_mu;
+  HostCopyStreams *per_dev = g_copy_per_dev;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
@@ -43,6 +46,26 @@ HostCopyStreams *streams_for_current_device() {
 }
 
 }  // namespace
+
+// Destroys the staging streams and events of device `dev` (before a device
+// reset, which would leave their handles dangling).
+void host_copy_release_streams(int dev) {
+  if (dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lock(g_copy_mu);
+  HostCopyStreams &s = g_copy_per_dev[dev];
+  if (!s.ok) return;
+  cudaStreamDestroy(s.h2d);
+  cudaStreamDestroy(s.comp);
+  cudaStreamDestroy(s.d2h);
+  for (int i = 0; i < kMaxSlots; ++i) {
+    cudaEventDestroy(s.in_ready[i]);
+    cudaEventDestroy(s.out_ready[i]);
+    cudaEventDestroy(s.in_free[i]);
+    cudaEventDestroy(s.out_free[i]);
+  }
+  s = HostCopyStreams{};
+}
+
 }  // namespace cmb
 
 using namespace cmb;

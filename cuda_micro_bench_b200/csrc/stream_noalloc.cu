@@ -9,8 +9,6 @@
 // cmb_stream_sum_f32_noalloc keeps that workspace in a file-scope device
 // array of fixed size instead.  It runs the same kernel with the same launch
 // shape, so its result equals cmb_stream_sum_f32's for the same input.
-#include <mutex>
-
 #include "cmb_device.cuh"
 #include "cmb_host.h"
 
@@ -31,28 +29,21 @@ constexpr size_t kNoAllocScratchBytes = 256 + sizeof(double) * kNoAllocMaxCtas;
 // Every call on a device shares it.
 static __device__ __align__(256) unsigned char g_sum_scratch[kNoAllocScratchBytes];
 
-// Device address of g_sum_scratch, looked up once per device.  In host code
-// the symbol is only a stand-in; a kernel must be given this address.
+// Device address of g_sum_scratch in the current context.  In host code the
+// symbol is only a stand-in; a kernel must be given this address.  It is
+// looked up on every call rather than cached: after cudaDeviceReset() (or
+// with another context current) the runtime loads the module again and the
+// array can sit at a different address.  The lookup is a host-side table
+// read once the module is loaded.
 void *scratch_address_for_current_device(int *err) {
-  static std::mutex mu;
-  static void *addr[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    *err = fail(CMB_ERR_CUDA, "cmb_stream_sum_f32_noalloc: no current device");
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_sum_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    *err = fail(CMB_ERR_CUDA, "cmb_stream_sum_f32_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(e));
     return nullptr;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_sum_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      *err = fail(CMB_ERR_CUDA, "cmb_stream_sum_f32_noalloc: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(e));
-      return nullptr;
-    }
-    addr[dev] = p;
-  }
-  return addr[dev];
+  return p;
 }
 
 }  // namespace

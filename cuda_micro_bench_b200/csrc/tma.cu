@@ -311,20 +311,23 @@ __global__ void __launch_bounds__(kLsuThreads)
   }
 }
 
-__global__ void k_tma_1d_latency(const __grid_constant__ CUtensorMap map, int iters,
-                                 uint32_t *out_cycles, int *status) {
+__global__ void k_tma_1d_latency(const __grid_constant__ CUtensorMap map, int x, int iters,
+                                 uint32_t *out_cycles, uint8_t *landed, int *status) {
   __shared__ __align__(128) uint8_t buf[128];
   __shared__ __align__(8) uint64_t bar;
   if (threadIdx.x != 0) return;
   const uint32_t b = dev::smem_addr(&bar);
   dev::mbar_init(b, 1);
   dev::fence_mbar_init();
+  // The destination starts zeroed, so the bytes read back after the loop
+  // can only have come from the loads.
+  reinterpret_cast<uint4 *>(buf)[0] = make_uint4(0u, 0u, 0u, 0u);
   dev::fence_proxy_async_smem();
   uint32_t done = 0;
   const uint64_t t0 = dev::clock64();
   for (int i = 0; i < iters; ++i) {
     dev::mbar_arrive_expect_tx(b, 16);
-    dev::tma_load_1d(dev::smem_addr(buf), &map, 0, b);
+    dev::tma_load_1d(dev::smem_addr(buf), &map, x, b);
     if (!dev::mbar_wait_bounded(b, static_cast<uint32_t>(i & 1))) {
       dev::report_status(status, CMB_ERR_TIMEOUT);
       // the load may still land: wait once more before leaving
@@ -335,6 +338,7 @@ __global__ void k_tma_1d_latency(const __grid_constant__ CUtensorMap map, int it
   }
   const uint64_t t1 = dev::clock64_after(done + buf[0]);
   *out_cycles = static_cast<uint32_t>(t1 - t0);
+  if (landed != nullptr) reinterpret_cast<uint4 *>(landed)[0] = reinterpret_cast<const uint4 *>(buf)[0];
 }
 
 template <int STAGES>
@@ -463,12 +467,21 @@ extern "C" int cmb_tma_tile_load_bf16(const void *src, int rows, int cols, int b
                    0, stream);
 }
 
-extern "C" int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint32_t *out_cycles,
-                                  int *status, cmb_stream_t stream) {
+extern "C" int cmb_tma_1d_latency(const void *buf, size_t bytes, size_t offset, int iters,
+                                  uint32_t *out_cycles, uint8_t *landed, int *status,
+                                  cmb_stream_t stream) {
   if (buf == nullptr || out_cycles == nullptr || iters <= 0)
     return fail(CMB_ERR_INVALID_ARG, "cmb_tma_1d_latency: null buffer/output or iters <= 0");
   if (bytes < 16 || (reinterpret_cast<uintptr_t>(buf) & 15))
     return fail(CMB_ERR_INVALID_ARG, "cmb_tma_1d_latency: need >= 16 bytes, 16-byte aligned");
+  // The load's x coordinate (bytes) must be 16-byte aligned, and the 16
+  // bytes must lie inside the buffer.
+  if ((offset & 15) != 0 || offset > bytes - 16 || offset > 0x7FFFFFF0u)
+    return fail(CMB_ERR_INVALID_ARG,
+                "cmb_tma_1d_latency: offset %zu not a multiple of 16 inside %zu bytes", offset,
+                bytes);
+  if (landed != nullptr && (reinterpret_cast<uintptr_t>(landed) & 15))
+    return fail(CMB_ERR_INVALID_ARG, "cmb_tma_1d_latency: landed not 16-byte aligned");
   EncodeTiledFn enc = encode_tiled_fn();
   if (enc == nullptr) return fail(CMB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   CUtensorMap map;
@@ -482,7 +495,8 @@ extern "C" int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint
   if (r != CUDA_SUCCESS) return fail(CMB_ERR_INVALID_ARG, "cuTensorMapEncodeTiled 1-D failed (%d)",
                                      static_cast<int>(r));
   if (status != nullptr) CMB_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), stream));
-  k_tma_1d_latency<<<1, 32, 0, stream>>>(map, iters, out_cycles, status);
+  k_tma_1d_latency<<<1, 32, 0, stream>>>(map, static_cast<int>(offset), iters, out_cycles, landed,
+                                         status);
   CMB_LAUNCH_CHECK();
   return CMB_OK;
 }

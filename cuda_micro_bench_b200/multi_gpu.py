@@ -11,7 +11,11 @@ collective library.
 Plans (all offsets in bytes):
   ring:      rank r sends its whole buffer to rank (r + 1) % N.
   alltoall:  the buffer is N chunks; rank r sends chunk j to rank j, which
-             stores it at chunk position r (chunk r stays local).
+             stores it at chunk position r (chunk r stays local).  Rank r
+             lists its jobs staggered, peers r+1, r+2, ... first and its own
+             chunk last, so at every position of the job list each rank
+             receives from exactly one sender (the order the copy engines
+             visit them when the jobs share one stream).
 """
 
 import ctypes
@@ -44,7 +48,8 @@ def plan(mode: str, rank: int, world: int, nbytes: int) -> List[Job]:
         return [Job(0, (rank + 1) % world, 0, nbytes)]
     if mode == "alltoall":
         c = chunk_bytes(world, nbytes)
-        return [Job(j * c, j, rank * c, c) for j in range(world)]
+        order = [(rank + 1 + k) % world for k in range(world)]
+        return [Job(j * c, j, rank * c, c) for j in order]
     raise ValueError(mode)
 
 
@@ -118,6 +123,10 @@ class PeerExchange:
             self.capi.check("cmb_p2p_scatter_bulk", dst, src, nb, n, 0, None, stream)
         elif method == "copy_engine":
             self.capi.check("cmb_p2p_scatter_copy_engine", dst, src, nb, n, stream)
+        elif method == "copy_engine_1stream":
+            self.capi.check("cmb_p2p_scatter_copy_engine_tuned", dst, src, nb, n, 1, stream)
+        elif method == "copy_engine_2stream":
+            self.capi.check("cmb_p2p_scatter_copy_engine_tuned", dst, src, nb, n, 2, stream)
         else:
             raise ValueError(method)
 

@@ -51,6 +51,15 @@ const char *cmb_status_string(int status);
 const char *cmb_last_error(void);
 /* Library version string. */
 const char *cmb_version(void);
+/* cudaDeviceReset() of the current device in the library's own CUDA
+ * runtime, after releasing the streams and events the library keeps for
+ * that device.  The library links the CUDA runtime statically, so a
+ * caller's cudaDeviceReset() reaches only the caller's runtime; a process
+ * that resets a device it used through this library calls this as well.
+ * Every device allocation made through the library on that device is
+ * gone afterwards.  No reference counterpart (the reference is one
+ * executable with one runtime). */
+int cmb_device_reset(void);
 
 /* --- seeded input generators (not part of any timed region) ---------- */
 
@@ -102,12 +111,12 @@ int cmb_stream_sum_f32(const float *src, size_t n, double *out_sum, void *worksp
  * launches up to 4 CTAs per SM, so any n fits on GPUs of up to 1024 SMs;
  * a GPU that would need more returns CMB_ERR_INVALID_ARG.  Nothing is
  * allocated: no cudaMalloc, cudaFree or allocating library call.
- * The first call on a device looks up the array's device address (once per
- * device, with that device current).  All calls on a device share the
- * array: calls that overlap on
- * the GPU (other streams, or other host threads) race and give wrong sums;
- * serialise them.  The result equals cmb_stream_sum_f32's for the same
- * input. */
+ * Every call looks up the array's device address in the current context
+ * (cudaGetSymbolAddress), so a call after cmb_device_reset() uses the
+ * reloaded array.  All calls on a device share the array: calls that
+ * overlap on the GPU (other streams, or other host threads) race and give
+ * wrong sums; serialise them.  The result equals cmb_stream_sum_f32's for
+ * the same input. */
 int cmb_stream_sum_f32_noalloc(const float *src, size_t n, double *out_sum, cmb_stream_t stream);
 /* Capacity of that array in per-CTA partials (4096). */
 size_t cmb_stream_sum_noalloc_max_ctas(void);
@@ -185,11 +194,16 @@ int cmb_tma_tile_copy_tuned(void *dst, const void *src, int rows, int cols, int 
 int cmb_tma_tile_load_bf16(const void *src, int rows, int cols, int box_rows, int box_cols,
                            int stages, uint32_t *xor_out, size_t xor_words, int *status,
                            cmb_stream_t stream);
-/* One thread issues `iters` 16-byte 1-D TMA loads of buf, waiting for each;
- * *out_cycles (device) = SM cycles of the loop.  Replaces
- * kernel_tma_1d_latency (src/tma.cu:20-69). */
-int cmb_tma_1d_latency(const void *buf, size_t bytes, int iters, uint32_t *out_cycles,
-                       int *status, cmb_stream_t stream);
+/* One thread issues `iters` 16-byte 1-D TMA loads of buf[offset:offset+16)
+ * into the same zeroed shared-memory slot, waiting for each; *out_cycles
+ * (device) = SM cycles of the loop; landed (device, 16 bytes, 16-byte
+ * aligned, may be NULL) = the 16 bytes in shared memory after the last
+ * load, which must equal buf[offset:offset+16).  offset is a multiple of
+ * 16 with offset + 16 <= bytes (the TMA coordinate's alignment rule).
+ * Replaces kernel_tma_1d_latency (src/tma.cu:20-69), which loads from
+ * coordinate 0 and keeps no output. */
+int cmb_tma_1d_latency(const void *buf, size_t bytes, size_t offset, int iters,
+                       uint32_t *out_cycles, uint8_t *landed, int *status, cmb_stream_t stream);
 
 /* --- tcgen05 dense GEMM (src/tensor_core.cu, src/tensor_core_extended.cu)  */
 
@@ -321,6 +335,14 @@ int cmb_p2p_scatter_bulk_tuned(void *const *dst, const void *const *src, const s
  * stream per job, joined back into `stream`). */
 int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src, const size_t *bytes,
                                 int n, cmb_stream_t stream);
+/* cmb_p2p_scatter_copy_engine over `streams` (1..8) internal streams: job j
+ * runs on stream j % streams, after the earlier jobs of that stream, so the
+ * order of the jobs is the order each stream visits its destinations (an
+ * all-to-all whose ranks start at different peers keeps every receiver
+ * busy with one sender at a time). */
+int cmb_p2p_scatter_copy_engine_tuned(void *const *dst, const void *const *src,
+                                      const size_t *bytes, int n, int streams,
+                                      cmb_stream_t stream);
 
 /* --- self-test of the bounded-wait rule -------------------------------- */
 
@@ -342,13 +364,24 @@ int cmb_compare_bytes(const void *a, const void *b, size_t bytes,
  * Each runs one section on device 0 like the reference's
  * `void cmb::benchmark_<section>()`: allocates, checks outputs, times, and
  * logs into the results table under the reference's keys (plus new ones);
- * returns a status instead of exiting. */
+ * returns a status instead of exiting.
+ * The library also exports, with C++ linkage, the reference's own
+ *   void cmb::benchmark_global_memory(), cmb::benchmark_cache(),
+ *   cmb::benchmark_tma(), cmb::benchmark_tensor_core(),
+ *   cmb::benchmark_tensor_core_extended(), cmb::benchmark_multi_gpu()
+ * (src/main.cu:9-32), which exit(EXIT_FAILURE) on a failure as the
+ * reference's sections do, so the reference's main.cu links against the
+ * library in place of its mem_global.cu, memory_chase.cu, mem_cache.cu,
+ * tma.cu, tensor_core.cu and tensor_core_extended.cu.  No other C++ symbol
+ * is exported. */
 int cmb_benchmark_global_memory(void);       /* src/mem_global.cu:27-75 */
 int cmb_benchmark_cache(void);               /* src/mem_cache.cu:4-24 */
 int cmb_benchmark_tma(void);                 /* src/tma.cu:157-259 */
 int cmb_benchmark_tensor_core(void);         /* src/tensor_core.cu:66-120 */
 int cmb_benchmark_tensor_core_extended(void);  /* src/tensor_core_extended.cu:321-357 */
 int cmb_benchmark_multi_gpu(void);           /* new: NVLink P2P and sharded stream */
+int cmb_benchmark_memory_more(void);         /* src/memory_more.cu:201-234 (L2 bandwidth only) */
+int cmb_benchmark_pcie(void);                /* src/pcie.cu:55-97 (pinned bandwidth only) */
 /* Logs "N/A" for every key the reference's results/report.html reads that
  * no section logged, so the report renders. */
 int cmb_results_log_report_placeholders(void);
@@ -374,6 +407,23 @@ int cmb_results_log(const char *section, const char *key, double value, const ch
 int cmb_results_write_json(const char *path);
 /* Empties the table and the device fields. */
 int cmb_results_clear(void);
+
+/* Callbacks that receive every entry the library's table receives. */
+typedef void (*cmb_results_log_fn)(const char *section, const char *key, double value,
+                                   const char *unit, void *user);
+typedef void (*cmb_results_device_fn)(const char *name, const char *arch, int sm_count,
+                                      int clock_khz, int mem_clock_khz, int mem_bus_width,
+                                      void *user);
+/* From now on every ResultLogger::log / setDevice the library makes (its
+ * sections and cmb_results_log / cmb_results_set_device) is also passed to
+ * `log` / `device` (either may be NULL; both NULL uninstalls), one call at a
+ * time, on the thread that logged.  This is how the library's sections log
+ * into the reference's own cmb::g_results (include/result_logger.h:111-144)
+ * when it is linked into the reference's main.cu: the library keeps its own
+ * table private, and a shim in the reference build forwards each call to
+ * g_results.log() and g_results.setDevice().  The callbacks must not call
+ * the library's cmb_results_* functions.  No reference counterpart. */
+int cmb_results_set_sink(cmb_results_log_fn log, cmb_results_device_fn device, void *user);
 
 #ifdef __cplusplus
 }

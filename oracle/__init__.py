@@ -12,13 +12,18 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 REF_LOGGER = os.path.join(HERE, "_ref", "ref_logger")
+REF_DROPIN = os.path.join(HERE, "_ref", "ref_dropin")
 
 _lib = None
 
 
-def build(ref: bool = False) -> None:
-    targets = ["all"] + (["ref"] if ref else [])
-    proc = subprocess.run(["make", "-C", HERE, *targets], stdout=subprocess.PIPE,
+def build(ref: bool = False, ref_root: str = None) -> None:
+    """make all; with ref=True also the test builds of the reference's own
+    sources (its result logger and its main.cu against libcmb_b200.so), read
+    from ref_root (default: the Makefile's)."""
+    targets = ["all"] + (["ref", "ref-dropin"] if ref else [])
+    extra = [f"REF_ROOT={ref_root}"] if ref_root else []
+    proc = subprocess.run(["make", "-C", HERE, "-j8", *targets, *extra], stdout=subprocess.PIPE,
                           stderr=subprocess.STDOUT, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{proc.stdout}")
@@ -53,6 +58,7 @@ def load():
         "orc_amax_bf16": (f, [p, sz]),
         "orc_quantize_e4m3": (None, [p, sz, f, p]),
         "orc_gemm_tile_f64": (None, [p, p, i, i, i, i, i, i, i, i, d, d, p]),
+        "orc_gemm_tiles_f64": (None, [p, p, i, i, i, i, i, p, d, d, p, i]),
         "orc_gemm_bf16_rows_f32": (None, [p, p, p, i, i, i, i, i]),
     }
     for name, (res, args) in sig.items():

@@ -308,6 +308,123 @@ void orc_gemm_tile_f64(const void *A, const void *B, int dtype, int K, int lda,
   free(bt);
 }
 
+/* Sampled-tile check (orc_gemm_tiles_f64): the tile's B columns are decoded
+ * once into k-major doubles, then threads take blocks of four output rows;
+ * each block keeps 4 x 32 accumulators and walks k in order, so every
+ * element is the same k-ordered sum orc_gemm_tile_f64 forms. */
+typedef struct {
+  const void *A;
+  const double *bt; /* K x tn, k-major */
+  double *out;
+  int dtype, K, lda, row0, tm, tn;
+  double scale_a;
+  int next; /* next row block, taken under mu */
+  pthread_mutex_t mu;
+} tiles_job;
+
+__attribute__((target_clones("arch=x86-64-v4", "arch=x86-64-v3", "default")))
+static void *tiles_worker(void *p) {
+  tiles_job *g = (tiles_job *)p;
+  enum { RB = 4, CB = 32 };
+  const int K = g->K;
+  double *a = (double *)malloc(sizeof(double) * RB * (size_t)K);
+  for (;;) {
+    pthread_mutex_lock(&g->mu);
+    const int r0 = g->next;
+    g->next += RB;
+    pthread_mutex_unlock(&g->mu);
+    if (r0 >= g->tm) break;
+    const int rb = g->tm - r0 < RB ? g->tm - r0 : RB;
+    for (int q = 0; q < RB; ++q)
+      for (int k = 0; k < K; ++k) {
+        double v = 0.0;
+        if (q < rb) {
+          const size_t o = (size_t)(g->row0 + r0 + q) * g->lda + k;
+          v = g->dtype == 0 ? (double)orc_bf16_to_f32(((const uint16_t *)g->A)[o])
+                            : (double)orc_e4m3_to_f32(((const uint8_t *)g->A)[o]) * g->scale_a;
+        }
+        a[(size_t)q * K + k] = v;
+      }
+    for (int c0 = 0; c0 < g->tn; c0 += CB) {
+      const int cb = g->tn - c0 < CB ? g->tn - c0 : CB;
+      double acc[RB][CB];
+      for (int q = 0; q < RB; ++q)
+        for (int c = 0; c < CB; ++c) acc[q][c] = 0.0;
+      if (cb == CB) {
+        for (int k = 0; k < K; ++k) {
+          const double *b = g->bt + (size_t)k * g->tn + c0;
+          const double a0 = a[k], a1 = a[K + k], a2 = a[2 * (size_t)K + k],
+                       a3 = a[3 * (size_t)K + k];
+          for (int c = 0; c < CB; ++c) {
+            acc[0][c] += a0 * b[c];
+            acc[1][c] += a1 * b[c];
+            acc[2][c] += a2 * b[c];
+            acc[3][c] += a3 * b[c];
+          }
+        }
+      } else {
+        for (int k = 0; k < K; ++k) {
+          const double *b = g->bt + (size_t)k * g->tn + c0;
+          for (int q = 0; q < RB; ++q)
+            for (int c = 0; c < cb; ++c) acc[q][c] += a[(size_t)q * K + k] * b[c];
+        }
+      }
+      for (int q = 0; q < rb; ++q)
+        for (int c = 0; c < cb; ++c) g->out[(size_t)(r0 + q) * g->tn + c0 + c] = acc[q][c];
+    }
+  }
+  free(a);
+  return NULL;
+}
+
+/* Decodes B columns [col0, col0 + tn) into k-major doubles; thread `part`
+ * of `parts` takes the k rows part, part + parts, ... */
+typedef struct {
+  const void *B;
+  double *bt;
+  int dtype, K, ldb, col0, tn, part, parts;
+  double scale_b;
+} decode_job;
+
+static void *decode_worker(void *p) {
+  const decode_job *d = (const decode_job *)p;
+  for (int k = d->part; k < d->K; k += d->parts)
+    for (int j = 0; j < d->tn; ++j) {
+      const size_t o = (size_t)(d->col0 + j) * d->ldb + k;
+      d->bt[(size_t)k * d->tn + j] =
+          d->dtype == 0 ? (double)orc_bf16_to_f32(((const uint16_t *)d->B)[o])
+                        : (double)orc_e4m3_to_f32(((const uint8_t *)d->B)[o]) * d->scale_b;
+    }
+  return NULL;
+}
+
+void orc_gemm_tiles_f64(const void *A, const void *B, int dtype, int K, int lda, int ldb,
+                        int ntiles, const int *tiles, double scale_a, double scale_b,
+                        double *out, int threads) {
+  const int t = pick_threads(threads);
+  const int nt = t < 256 ? t : 256;
+  pthread_t th[256];
+  decode_job dj[256];
+  size_t off = 0;
+  for (int i = 0; i < ntiles; ++i) {
+    const int row0 = tiles[4 * i], col0 = tiles[4 * i + 1];
+    const int tm = tiles[4 * i + 2], tn = tiles[4 * i + 3];
+    double *bt = (double *)malloc(sizeof(double) * (size_t)K * tn);
+    for (int k = 0; k < nt; ++k) {
+      dj[k] = (decode_job){B, bt, dtype, K, ldb, col0, tn, k, nt, scale_b};
+      pthread_create(&th[k], NULL, decode_worker, &dj[k]);
+    }
+    for (int k = 0; k < nt; ++k) pthread_join(th[k], NULL);
+    tiles_job g = {A, bt, out + off, dtype, K, lda, row0, tm, tn, scale_a, 0,
+                   PTHREAD_MUTEX_INITIALIZER};
+    for (int k = 0; k < nt; ++k) pthread_create(&th[k], NULL, tiles_worker, &g);
+    for (int k = 0; k < nt; ++k) pthread_join(th[k], NULL);
+    pthread_mutex_destroy(&g.mu);
+    free(bt);
+    off += (size_t)tm * tn;
+  }
+}
+
 typedef struct {
   const uint16_t *A, *B;
   float *C;

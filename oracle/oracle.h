@@ -86,6 +86,14 @@ void orc_quantize_e4m3(const uint16_t *x, size_t n, float inv_scale, uint8_t *q)
 void orc_gemm_tile_f64(const void *A, const void *B, int dtype, int K,
                        int lda, int ldb, int row0, int col0, int tm, int tn,
                        double scale_a, double scale_b, double *out);
+/* orc_gemm_tile_f64 on `ntiles` tiles at once over host threads (threads
+ * <= 0: all).  tiles holds (row0, col0, tm, tn) per tile; the tiles' outputs
+ * are stored one after another in out (tile t at the sum of the earlier
+ * tiles' tm * tn), each tm x tn row-major.  Every output element is summed
+ * in k order, as in orc_gemm_tile_f64. */
+void orc_gemm_tiles_f64(const void *A, const void *B, int dtype, int K, int lda, int ldb,
+                        int ntiles, const int *tiles, double scale_a, double scale_b,
+                        double *out, int threads);
 /* Blocked fp32 GEMM over host threads (the CPU baseline's timed kernel);
  * computes rows [row0, row0 + rows) of C = A * B^T for bf16 A, B, written
  * as a rows x N row-major block at C.  Threads split the output columns. */

@@ -56,7 +56,13 @@ SCRIPTS = {
 }
 
 
-REPORT = "/root/reference/results/report.html"
+# The reference checkout's report: CMB_REFERENCE_ROOT, or the `reference`
+# directory beside this repository.
+REPORT = os.path.join(
+    os.environ.get("CMB_REFERENCE_ROOT")
+    or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__))))), "reference"),
+    "results", "report.html")
 
 
 def report_keys():

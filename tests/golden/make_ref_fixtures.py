@@ -11,9 +11,10 @@ ref_gpu_fixtures.json
     hmma_*_sum_iters1000  kernel_hmma_{bf16,int8}_throughput outputs (sum of a
                           thread's four accumulators after 1000 all-ones MMAs)
 
-Run on a GPU box (the binary is built here, where the reference tree is):
-    python tests/golden/make_ref_fixtures.py gpurun_out/ref_gpu_fixtures.json
-then copy the output next to this script.
+Run on a machine with a B200, with the binary built beforehand where the
+reference sources are:
+    python tests/golden/make_ref_fixtures.py OUT.json
+and store OUT.json next to this script as ref_gpu_fixtures.json.
 """
 
 import os

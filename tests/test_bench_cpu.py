@@ -50,3 +50,20 @@ def test_argument_checks():
     assert p.returncode != 0 and "--steps must be >= 1" in p.stderr
     p = _run("--gpus", "2")
     assert p.returncode != 0 and "torchrun" in p.stderr
+
+
+def test_failed_checks_finds_every_failed_probe_flag():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    probes = {"stream_1gib": {"copy": {"bit_exact": True, "status": 0}},
+              "gemm": {"bf16": {"within_1e-2": False, "status": 0},
+                       "cublas_same_operands": {"bf16_TFLOP/s": 1500.0}},
+              "tma_16384": {"tma_1d": {"landed_bytes_match": True, "status": 3}},
+              "p2p_256mib": {"ring_store": {"bit_exact": False},
+                             "nccl_reference": {"ring_nccl": {"received_first_chunk_ok": False}}},
+              "chase_512mib": {"endpoint_matches_host_walk": True}}
+    assert sorted(bench.failed_checks(probes)) == [
+        "gemm.bf16.within_1e-2=False", "p2p_256mib.ring_store.bit_exact=False",
+        "tma_16384.tma_1d.status=3"]
+    assert bench.failed_checks({"a": {"bit_exact": True, "status": 0}}) == []

@@ -1,6 +1,10 @@
 """GPU parity of the tcgen05 GEMM probes against the oracle's fp64 GEMM
-(stated tolerance: per checked tile, max |C - C_ref| <= 1e-2 * max |C_ref|),
-and of the e4m3 quantiser against the oracle's encoder (bit-exact)."""
+(stated tolerance: per checked tile, max |C - C_ref| <= 1e-2 * max |C_ref|,
+the max-norm reading of "rel tol 1e-2"), and of the e4m3 quantiser against
+the oracle's encoder (bit-exact).  The 8192^3 configuration is checked on 64
+sampled 256 x 256 output tiles (the two corner tiles included) of every
+variant the bench reports: bf16 and e4m3, fp32 and bf16 C, 1-CTA 128 x 256,
+2-CTA 256 x 512 and 2-CTA 256 x 256 tiles."""
 
 import ctypes
 
@@ -37,16 +41,33 @@ def _gemm(cuda, cmb, fn, A, B, M, N, K, cg, scales=None):
 
 
 def _check_tiles(orc, A_h, B_h, C, K, tiles, dtype=0, sa=1.0, sb=1.0):
-    worst = 0.0
+    """Max over `tiles` of the per-tile max-norm relative error against the
+    oracle's fp64 GEMM (all tiles computed at once on the host's threads)."""
+    spec = np.array(tiles, np.int32).reshape(-1, 4)
+    ref_all = np.empty(int((spec[:, 2].astype(np.int64) * spec[:, 3]).sum()), np.float64)
+    orc.orc_gemm_tiles_f64(ptr(A_h), ptr(B_h), dtype, K, K, K, len(spec), ptr(spec), sa, sb,
+                           ptr(ref_all), 0)
+    worst, off = 0.0, 0
     for (r0, c0, tm, tn) in tiles:
-        ref = np.empty((tm, tn), np.float64)
-        orc.orc_gemm_tile_f64(ptr(A_h), ptr(B_h), dtype, K, K, K, r0, c0, tm, tn, sa, sb, ptr(ref))
+        ref = ref_all[off:off + tm * tn].reshape(tm, tn)
+        off += tm * tn
         got = C[r0:r0 + tm, c0:c0 + tn].astype(np.float64)
         assert np.isfinite(got).all()
         err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
         worst = max(worst, err)
         assert err <= RTOL, (r0, c0, err)
     return worst
+
+
+def config_tiles(M, N, seed, count=64, size=256):
+    """`count` sampled size x size output tiles on a size-aligned grid: the
+    first and the last corner tile, the rest drawn from `seed`."""
+    rng = np.random.default_rng(seed)
+    tiles = [(int(r) * size, int(c) * size, size, size)
+             for r, c in zip(rng.integers(0, M // size, count), rng.integers(0, N // size, count))]
+    tiles[0] = (0, 0, size, size)
+    tiles[1] = (M - size, N - size, size, size)
+    return tiles
 
 
 @pytest.mark.parametrize("cg", [1, 2])
@@ -64,7 +85,7 @@ def test_gemm_bf16_small_full_check(cuda, cmb, orc, cg, M, N, K):
 
 @pytest.mark.parametrize("cg", [1, 2])
 def test_gemm_bf16_8192_sampled_tiles(cuda, cmb, orc, cg):
-    """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5; 64 sampled 64x64 output
+    """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5; 64 sampled 256x256 output
     tiles against the fp64 oracle."""
     M = N = K = 8192
     A = _normal_bf16(cuda, cmb, M, K, 11, K ** -0.5)
@@ -72,12 +93,7 @@ def test_gemm_bf16_8192_sampled_tiles(cuda, cmb, orc, cg):
     C = _gemm(cuda, cmb, "bf16", A, B, M, N, K, cg)
     A_h = A.cpu().numpy().view(np.uint16)
     B_h = B.cpu().numpy().view(np.uint16)
-    rng = np.random.default_rng(cg)
-    tiles = [(int(r) * 64, int(c) * 64, 64, 64)
-             for r, c in zip(rng.integers(0, M // 64, 64), rng.integers(0, N // 64, 64))]
-    tiles[0] = (0, 0, 64, 64)
-    tiles[1] = (M - 64, N - 64, 64, 64)
-    worst = _check_tiles(orc, A_h, B_h, C, K, tiles)
+    worst = _check_tiles(orc, A_h, B_h, C, K, config_tiles(M, N, cg))
     assert worst < 1e-4
     assert np.isfinite(C).all()
 
@@ -116,13 +132,35 @@ def test_gemm_e4m3(cuda, cmb, orc, cg, M, N, K):
     C = _gemm(cuda, cmb, "e4m3", qa, qb, M, N, K, cg, scales=(sa[:1], sb[:1]))
     qa_h, qb_h = qa.cpu().numpy(), qb.cpu().numpy()
     sa_h, sb_h = float(sa[0].item()), float(sb[0].item())
-    if M * N <= 1 << 20:
-        tiles = [(0, 0, M, N)]
-    else:
-        rng = np.random.default_rng(7 + cg)
-        tiles = [(int(r) * 64, int(c) * 64, 64, 64)
-                 for r, c in zip(rng.integers(0, M // 64, 64), rng.integers(0, N // 64, 64))]
+    tiles = [(0, 0, M, N)] if M * N <= 1 << 20 else config_tiles(M, N, 7 + cg)
     _check_tiles(orc, qa_h, qb_h, C, K, tiles, dtype=1, sa=sa_h, sb=sb_h)
+
+
+@pytest.mark.parametrize("fp8", [0, 1])
+def test_gemm_8192_2cta_256x256_tile(cuda, cmb, orc, fp8):
+    """Config, with the configuration's literal 2-CTA 256 x 256 x 64 tile
+    (the bench's bf16_8192_2cta_256x256 line): two accumulators of 256
+    columns, 4 epilogue warps; 64 sampled 256x256 tiles against fp64."""
+    M = N = K = 8192
+    A = _normal_bf16(cuda, cmb, M, K, 71, K ** -0.5)
+    B = _normal_bf16(cuda, cmb, N, K, 72, K ** -0.5)
+    C = cuda.full((M * N,), float("nan"), dtype=cuda.float32, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    if fp8:
+        qa, sa = _quantize(cuda, cmb, A)
+        qb, sb = _quantize(cuda, cmb, B)
+        args = (dptr(qa), dptr(qb), dptr(C), M, N, K, 1, dptr(sa), dptr(sb))
+        a_h, b_h = qa.cpu().numpy(), qb.cpu().numpy()
+        s_a, s_b = float(sa[0].item()), float(sb[0].item())
+    else:
+        args = (dptr(A), dptr(B), dptr(C), M, N, K, 0, None, None)
+        a_h, b_h = A.cpu().numpy().view(np.uint16), B.cpu().numpy().view(np.uint16)
+        s_a = s_b = 1.0
+    cmb.check("cmb_gemm_tuned", *args, 2, 4, 8, 2, 256, 4, dptr(status), stream_handle(cuda))
+    cuda.cuda.synchronize()
+    assert int(status.item()) == 0
+    _check_tiles(orc, a_h, b_h, C.cpu().numpy().reshape(M, N), K, config_tiles(M, N, 9 + fp8),
+                 dtype=fp8, sa=s_a, sb=s_b)
 
 
 @pytest.mark.parametrize("fp8", [0, 1])
@@ -281,6 +319,8 @@ def test_gemm_bf16_out_is_the_rounded_fp32_result(cuda, cmb, orc, fp8, M, N, K, 
     out = Cb.float().cpu().numpy().reshape(M, N)
     if M * N <= 1 << 20:
         tiles = [(0, 0, M, N)]
+    elif M == N == 8192:
+        tiles = config_tiles(M, N, 13 + fp8)
     else:
         rng = np.random.default_rng(M + N)
         tiles = [(int(r) * 64, int(c) * 64, 64, 64)

@@ -58,6 +58,17 @@ def test_plans_any_world_and_size(mode, world, units):
     assert total_egress == expect
 
 
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_alltoall_plan_is_staggered(world):
+    """At every position of the job lists, each rank is the destination of
+    exactly one sender, and every rank's own chunk comes last."""
+    nbytes = 16 * world * 8
+    plans = [multi_gpu.plan("alltoall", r, world, nbytes) for r in range(world)]
+    for k in range(world):
+        assert sorted(p[k].dst_rank for p in plans) == list(range(world))
+    assert all(p[-1].dst_rank == r for r, p in enumerate(plans))
+
+
 def test_egress_bytes():
     n = 1 << 28
     for world in (2, 4, 8):

@@ -7,6 +7,7 @@ import ctypes
 import numpy as np
 import pytest
 
+from oracle import ptr
 from tests.helpers import dptr, stream_handle
 
 pytestmark = pytest.mark.gpu
@@ -94,16 +95,33 @@ def test_tile_load_xor(cuda, cmb):
     assert np.array_equal(got, expect)
 
 
-def test_tma_1d_latency(cuda, cmb):
-    buf = cuda.zeros(1024, dtype=cuda.uint8, device="cuda")
+@pytest.mark.parametrize("offset", [0, 16, 1008])
+def test_tma_1d_latency(cuda, cmb, orc, offset):
+    """The reference's 16-byte 1-D TMA round trip (src/tma.cu:20-69), 256
+    times into one zeroed shared-memory slot: the bytes left there must be
+    the source's bytes at the load's coordinate (seeded bytes, oracle)."""
+    buf = cuda.empty(1024, dtype=cuda.uint8, device="cuda")
+    cmb.check("cmb_fill_bytes", dptr(buf), 1024, ctypes.c_uint64(77), stream_handle(cuda))
     cyc = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    landed = cuda.zeros(16, dtype=cuda.uint8, device="cuda")
     status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
-    cmb.check("cmb_tma_1d_latency", dptr(buf), 1024, 256, dptr(cyc), dptr(status),
-              stream_handle(cuda))
+    cmb.check("cmb_tma_1d_latency", dptr(buf), 1024, offset, 256, dptr(cyc), dptr(landed),
+              dptr(status), stream_handle(cuda))
     cuda.cuda.synchronize()
     assert int(status.item()) == 0
+    ref = np.empty(1024, np.uint8)
+    orc.orc_fill_bytes(ptr(ref), 1024, 77)
+    assert np.array_equal(landed.cpu().numpy(), ref[offset:offset + 16])
     per = int(cyc.item()) / 256
     assert 50 < per < 20000, per
+
+
+def test_tma_1d_latency_rejects_unaligned_offset(cuda, cmb):
+    buf = cuda.zeros(1024, dtype=cuda.uint8, device="cuda")
+    cyc = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    s = stream_handle(cuda)
+    for off in (8, 1016, 1024):  # not a multiple of 16, or past the end
+        assert cmb.lib.cmb_tma_1d_latency(dptr(buf), 1024, off, 4, dptr(cyc), None, None, s) == 1
 
 
 @pytest.mark.parametrize("rows,cols,box,stages", [
