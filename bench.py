@@ -117,6 +117,10 @@ class ClockSampler:
                  f"-i", str(self.gpu_index), f"-lms", str(self.period_ms)],
                 stdout=self.file, stderr=subprocess.DEVNULL)
             self.t0 = time.time()
+            # nvidia-smi needs a moment before its first sample: wait for it
+            # (up to 2 s) so a short timed region is sampled from its start
+            while time.time() - self.t0 < 2.0 and os.path.getsize(self.file.name) == 0:
+                time.sleep(0.005)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -261,7 +265,7 @@ def run_ours(args) -> int:
     if not ok:
         raise SystemExit(f"rank {ranks.rank}: copy output differs from input")
 
-    clocks = ClockSampler(dev_index).start()
+    clocks = ClockSampler(dev_index, period_ms=5).start()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     ranks.barrier()
     torch.cuda.synchronize()
@@ -655,8 +659,51 @@ def probe_gemm(torch, stream, sh, peaks):
     live["what"] = ("torch.mm / torch._scaled_mm (cuBLASLt), same operands, fp32 C (and bf16 C "
                     "for the *_bf16out keys), timed alongside")
     out["cublas_same_operands"] = live
+    # Back to back for a fixed time with the SM clock sampled: the rate each
+    # kernel holds under the power cap, and the rate per GHz of the clock it
+    # ran at (the two GEMMs compared at equal clocks).
+    dev_index = torch.cuda.current_device()
+    ours_bf16 = lambda: check("cmb_gemm_bf16_out", ctypes.c_void_p(A.data_ptr()),
+                              ctypes.c_void_p(B.data_ptr()), ctypes.c_void_p(Cb.data_ptr()), M, N, K,
+                              0, None, None, ctypes.c_void_p(status.data_ptr()), sh)
+    ours_e4m3 = lambda: check("cmb_gemm_bf16_out", ctypes.c_void_p(qa.data_ptr()),
+                              ctypes.c_void_p(qb.data_ptr()), ctypes.c_void_p(Cb.data_ptr()), M, N, K,
+                              1, ctypes.c_void_p(sa.data_ptr()), ctypes.c_void_p(sb.data_ptr()),
+                              ctypes.c_void_p(status.data_ptr()), sh)
+    sustained = {}
+    try:
+        for label, fn in (("ours_bf16_bf16out", ours_bf16),
+                          ("cublas_bf16_bf16out", lambda: torch.mm(a16, b16.t())),
+                          ("ours_e4m3_bf16out", ours_e4m3),
+                          ("cublas_e4m3_bf16out", lambda: torch._scaled_mm(
+                              f8a, f8b.t(), scale_a=sa[0], scale_b=sb[0], out_dtype=torch.bfloat16))):
+            sustained[label] = _sustained(torch, stream, fn, flop, dev_index)
+        sustained["what"] = ("each GEMM (8192^3, bf16 C) back to back for ~1 s with nvidia-smi "
+                             "sampling the SM clock every 5 ms")
+    except (RuntimeError, TypeError) as e:
+        sustained["error"] = str(e).splitlines()[0][:200]
+    out["sustained_with_clocks"] = sustained
     del A, B, C, Cb, qa, qb, a16, b16, f8a, f8b
     return out
+
+
+def _sustained(torch, stream, fn, flop, dev_index, seconds=1.0):
+    """TFLOP/s of fn run back to back for about `seconds` (device time, CUDA
+    events), the median SM clock sampled meanwhile, and TFLOP/s per GHz."""
+    for _ in range(3):
+        fn()
+    ms = statistics.median(_time_launches(torch, stream, fn, 5))
+    reps = max(10, int(seconds * 1e3 / ms))
+    clocks = ClockSampler(dev_index, period_ms=5).start()
+    time.sleep(0.05)
+    t = _time_launches(torch, stream, fn, reps)
+    clk = clocks.stop()
+    tf = flop * reps / (sum(t) * 1e-3) / 1e12
+    res = {"TFLOP/s": round(tf, 1), "launches": reps, "sm_mhz": clk.get("sm_mhz"),
+           "power_w_max": clk.get("power_w_max"), "reasons": clk.get("reasons")}
+    if clk.get("sm_mhz"):
+        res["TFLOP/s_per_GHz"] = round(tf / (clk["sm_mhz"] / 1e3), 1)
+    return res
 
 
 def _nccl_reference(ranks, nbytes, reps=5, warm=2) -> dict:
