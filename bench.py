@@ -352,10 +352,51 @@ def run_e2e(args, ranks, torch, dev_a, dev_b, nbytes):
     ranks.barrier()
     total = ranks.max(local)
     value = ranks.world * 2.0 * nbytes * steps / total / 1e9
+    links = _host_link_rates(torch, ranks, host_src, host_dst, dev_a, dev_b, nbytes)
     del host_src, host_dst
     return {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": nbytes,
             "d2h_bytes_per_step": nbytes, "steps": steps,
-            "path": "cmb_stream_copy_host (pinned host -> device copy -> host, 64 MiB chunks)"}
+            "path": "cmb_stream_copy_host (pinned host -> device copy -> host, 64 MiB chunks)",
+            "host_links": links}
+
+
+def _host_link_rates(torch, ranks, host_src, host_dst, dev_a, dev_b, nbytes) -> dict:
+    """What the host side alone carries, all ranks at once: plain pinned
+    host->device, device->host and both directions together
+    (cudaMemcpyAsync through torch), aggregate GB/s of all ranks from the
+    max-over-ranks wall time.  The e2e leg cannot exceed the both-directions
+    rate; a rate that grows less than N-fold with N shows a shared host."""
+    stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    d_a, d_b = dev_a.view(torch.uint8), dev_b.view(torch.uint8)
+
+    def h2d():
+        d_a.copy_(host_src, non_blocking=True)
+
+    def d2h():
+        host_dst.copy_(d_b, non_blocking=True)
+
+    def both():
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            host_dst.copy_(d_b, non_blocking=True)
+        d_a.copy_(host_src, non_blocking=True)
+        stream.wait_stream(side)
+
+    out = {}
+    for name, fn, bytes_moved in (("h2d_GB/s", h2d, nbytes), ("d2h_GB/s", d2h, nbytes),
+                                  ("h2d_plus_d2h_GB/s", both, 2 * nbytes)):
+        torch.cuda.synchronize()
+        ranks.barrier()
+        t0 = time.perf_counter()
+        fn()
+        torch.cuda.synchronize()
+        local = time.perf_counter() - t0
+        ranks.barrier()
+        out[name] = round(ranks.world * bytes_moved / ranks.max(local) / 1e9, 2)
+    out["what"] = (f"{nbytes >> 20} MiB pinned copies per rank, all {ranks.world} ranks at once, "
+                   "aggregate")
+    return out
 
 
 # ---------------------------------------------------------------- probes
@@ -818,6 +859,41 @@ def probe_p2p(args, ranks) -> dict:
     return out
 
 
+def probe_cublas(torch, stream, sh, ours_tile256=False) -> dict:
+    """The live reference of the GEMM probe alone, for profiling it: cuBLAS
+    (torch.mm) on the configuration's 8192^3 bf16 operands, fp32 and bf16 C,
+    median of 9 launches after 3 warm-up launches each.  With ours_tile256,
+    the configuration's literal 2-CTA 256 x 256 tile of this library instead
+    (cmb_gemm_tuned, fp32 C)."""
+    from cuda_micro_bench_b200 import check
+
+    M = N = K = 8192
+    A = torch.empty(M * K, dtype=torch.int16, device="cuda")
+    B = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(A.data_ptr()), M * K, ctypes.c_uint64(SEED + 1),
+          ctypes.c_float(K ** -0.5), sh)
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(B.data_ptr()), N * K, ctypes.c_uint64(SEED + 2),
+          ctypes.c_float(K ** -0.5), sh)
+    a16, b16 = A.view(M, K).view(torch.bfloat16), B.view(N, K).view(torch.bfloat16)
+    flop = 2.0 * M * N * K
+    out = {}
+    if ours_tile256:
+        C = torch.empty(M * N, dtype=torch.float32, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ms = _median_ms(torch, stream, lambda: check(
+            "cmb_gemm_tuned", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
+            ctypes.c_void_p(C.data_ptr()), M, N, K, 0, None, None, 2, 4, 8, 0, 256, 4,
+            ctypes.c_void_p(status.data_ptr()), sh))
+        out["bf16_2cta_256x256_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+        out["status"] = int(status.item())
+        return out
+    ms = _median_ms(torch, stream, lambda: torch.mm(a16, b16.t(), out_dtype=torch.float32))
+    out["bf16_fp32out_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+    ms = _median_ms(torch, stream, lambda: torch.mm(a16, b16.t()))
+    out["bf16_bf16out_TFLOP/s"] = round(flop / (ms * 1e-3) / 1e12, 1)
+    return out
+
+
 def run_probe_only(args) -> int:
     """Runs only the named probes (for profiling) and prints their results."""
     import torch
@@ -836,6 +912,10 @@ def run_probe_only(args) -> int:
             out["tma_16384"] = probe_tma(torch, stream, sh, peaks)
         elif name == "gemm":
             out["gemm"] = probe_gemm(torch, stream, sh, peaks)
+        elif name == "cublas":
+            out["cublas_8192"] = probe_cublas(torch, stream, sh)
+        elif name == "gemm256":
+            out["gemm_256x256"] = probe_cublas(torch, stream, sh, ours_tile256=True)
         torch.cuda.empty_cache()
     print(json.dumps({"probes": out}), flush=True)
     return 0
@@ -945,7 +1025,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick-chase", action="store_true",
                     help="2^22 chase hops instead of the configuration's 2^24")
-    ap.add_argument("--probe", action="append", choices=["stream", "chase", "tma", "gemm"],
+    ap.add_argument("--probe", action="append",
+                    choices=["stream", "chase", "tma", "gemm", "cublas", "gemm256"],
                     help="run only this probe (repeatable); no headline line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
