@@ -321,7 +321,11 @@ int cmb_p2p_scatter_store_tuned(void *const *dst, const void *const *src, const 
  * store.  16-byte aligned pointers; ctas_per_job <= 0 picks 32 (at most
  * SMs / n), which on a ring reach the same NVLink rate as peer stores from
  * every SM; *status (device, may be NULL) = CMB_ERR_TIMEOUT if a chunk
- * load never completed within 2 s.  No reference counterpart (new NVLink
+ * load never completed within 2 s.  After such a timeout a CTA issues no
+ * further loads and waits up to 0.1 s for each load still in flight; if one
+ * of those never lands either, the CTA exits with it outstanding, so a
+ * CMB_ERR_TIMEOUT from this call means the context must be treated as
+ * unusable (reset the device).  No reference counterpart (new NVLink
  * probe). */
 int cmb_p2p_scatter_bulk(void *const *dst, const void *const *src, const size_t *bytes, int n,
                          int ctas_per_job, int *status, cmb_stream_t stream);
