@@ -102,21 +102,26 @@ def _free_port():
     return port
 
 
-def _rank(rank, world, port, q):
+ALL_METHODS = ("store", "bulk", "copy_engine", "copy_engine_1stream", "copy_engine_2stream")
+
+
+def _rank(rank, world, port, q, device=None, backend="nccl"):
+    device = rank if device is None else device
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
-                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank), "NCCL_NVLS_ENABLE": "0"})
+                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(device),
+                       "NCCL_NVLS_ENABLE": "0"})
     import torch
 
-    torch.cuda.set_device(rank)
+    torch.cuda.set_device(device)
     import bench
     from cuda_micro_bench_b200 import multi_gpu
 
-    ranks = bench.Ranks("nccl")
+    ranks = bench.Ranks(backend)
     ex = multi_gpu.PeerExchange(ranks, 16 << 20, 77)
     bad = {}
     sh = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for mode in ("ring", "alltoall"):
-        for method in ("store", "bulk", "copy_engine"):
+        for method in ALL_METHODS:
             ranks.barrier()
             ex.launch(mode, method, sh)
             torch.cuda.synchronize()
@@ -143,4 +148,27 @@ def test_two_process_ipc_exchange(cuda):
         p.join(timeout=120)
         assert p.exitcode == 0
     for rank, bad in res:
+        assert all(v == 0 for v in bad.values()), (rank, bad)
+
+
+def test_two_process_ipc_exchange_on_one_gpu(cuda):
+    """The same two-rank exchange with both ranks on GPU 0 (gloo for the
+    host side): every receive buffer is another process's CUDA IPC mapping,
+    written by the peer-store and bulk-copy kernels and the copy engines
+    exactly as across NVLink, and checked bit for bit.  The kernels never wait
+    on each other; the host barriers order the steps."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, 0, "gloo")) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, bad in res:
+        assert len(bad) == 2 * len(ALL_METHODS)
         assert all(v == 0 for v in bad.values()), (rank, bad)
