@@ -410,15 +410,20 @@ void orc_gemm_tiles_f64(const void *A, const void *B, int dtype, int K, int lda,
     const int row0 = tiles[4 * i], col0 = tiles[4 * i + 1];
     const int tm = tiles[4 * i + 2], tn = tiles[4 * i + 3];
     double *bt = (double *)malloc(sizeof(double) * (size_t)K * tn);
+    int started = 0;
     for (int k = 0; k < nt; ++k) {
       dj[k] = (decode_job){B, bt, dtype, K, ldb, col0, tn, k, nt, scale_b};
-      pthread_create(&th[k], NULL, decode_worker, &dj[k]);
+      if (pthread_create(&th[started], NULL, decode_worker, &dj[k]) == 0) ++started;
+      else decode_worker(&dj[k]); /* no thread: decode this share here */
     }
-    for (int k = 0; k < nt; ++k) pthread_join(th[k], NULL);
+    for (int k = 0; k < started; ++k) pthread_join(th[k], NULL);
     tiles_job g = {A, bt, out + off, dtype, K, lda, row0, tm, tn, scale_a, 0,
                    PTHREAD_MUTEX_INITIALIZER};
-    for (int k = 0; k < nt; ++k) pthread_create(&th[k], NULL, tiles_worker, &g);
-    for (int k = 0; k < nt; ++k) pthread_join(th[k], NULL);
+    started = 0;
+    for (int k = 0; k < nt; ++k)
+      if (pthread_create(&th[started], NULL, tiles_worker, &g) == 0) ++started;
+    if (started == 0) tiles_worker(&g); /* every row block on this thread */
+    for (int k = 0; k < started; ++k) pthread_join(th[k], NULL);
     pthread_mutex_destroy(&g.mu);
     free(bt);
     off += (size_t)tm * tn;

@@ -202,3 +202,29 @@ def test_constant_mma_sums_pinned_to_reference_kernels():
     assert fx["stream_copy_1mib_identical"] is True
     assert fx["hmma_bf16_sum_iters1000"] == 4 * 16 * 1000
     assert fx["hmma_int8_sum_iters1000"] == 4 * 32 * 1000
+
+
+def test_gemm_tiles_f64_equals_single_tile_oracle(orc):
+    """The threaded multi-tile fp64 check sums every element in k order, so
+    it equals the single-tile oracle bit for bit (bf16 and e4m3 inputs,
+    ragged tile shapes)."""
+    rng = np.random.default_rng(5)
+    M, N, K = 300, 260, 200
+    for dtype in (0, 1):
+        if dtype == 0:
+            A = (rng.standard_normal(M * K).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+            B = (rng.standard_normal(N * K).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        else:
+            A = rng.integers(0, 0x7f, M * K, dtype=np.uint8)
+            B = rng.integers(0, 0x7f, N * K, dtype=np.uint8)
+        tiles = np.array([[0, 0, 64, 64], [13, 7, 37, 70], [M - 40, N - 33, 40, 33]], np.int32)
+        out = np.zeros(int((tiles[:, 2] * tiles[:, 3]).sum()))
+        orc.orc_gemm_tiles_f64(ptr(A), ptr(B), dtype, K, K, K, len(tiles), ptr(tiles), 0.5, 2.0,
+                               ptr(out), 3)
+        off = 0
+        for r0, c0, tm, tn in tiles:
+            ref = np.zeros(tm * tn)
+            orc.orc_gemm_tile_f64(ptr(A), ptr(B), dtype, K, K, K, int(r0), int(c0), int(tm),
+                                  int(tn), 0.5, 2.0, ptr(ref))
+            assert np.array_equal(out[off:off + tm * tn], ref), (dtype, r0, c0)
+            off += tm * tn
