@@ -38,6 +38,7 @@ SIGNATURES = {
     "cmb_stream_sum_f32_noalloc": (_i, [_p, _sz, _p, _p]),
     "cmb_stream_sum_noalloc_max_ctas": (_sz, []),
     "cmb_l2_read": (_i, [_p, _sz, _i, _i, _p, _p]),
+    "cmb_l2_read_bulk": (_i, [_p, _sz, _i, _p, _p, _p]),
     "cmb_stream_copy_host": (_i, [_p, _p, _sz, _p, _p, _sz, _sz]),
     "cmb_chase_build_links": (_i, [_p, _sz, _u64]),
     "cmb_chase_run": (_i, [_p, _sz, _u64, _u64, _i, _p, _p]),

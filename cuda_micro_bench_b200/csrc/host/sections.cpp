@@ -411,30 +411,49 @@ int section_memory_more() {
   DeviceInfo info;
   TRY(query_device(0, &info));
   printf("=== Memory (L2 aggregate bandwidth) ===\n");
-  const size_t bytes = std::min<size_t>(8ull << 20, (size_t)info.l2_cache_size / 4);
+  // 8 MiB (a multiple of the bulk path's 8 KiB chunks) stays in L2.
+  const size_t bytes = std::min<size_t>(8ull << 20, (size_t)info.l2_cache_size / 4) & ~size_t(8191);
   const int passes = 1024;
-  DevBuf buf, sum;
+  DevBuf buf, sum, st;
   TRY(buf.alloc(bytes));
   TRY(sum.alloc(sizeof(unsigned long long)));
+  TRY(st.alloc(sizeof(int)));
   TRY(cmb_fill_hash_u32(buf.as<uint32_t>(), bytes / 4, nullptr));
-  double ms = 0;
-  TRY(time_median([&] { return cmb_l2_read(buf.p, bytes, passes, 0, sum.as<unsigned long long>(), nullptr); },
-                  6, 1, &ms));
-  unsigned long long got = 0, words = 0;
-  CMB_CUDA_TRY(cudaMemcpy(&got, sum.p, sizeof(got), cudaMemcpyDeviceToHost));
+  unsigned long long words = 0;
   for (size_t i = 0; i < bytes / 4; ++i) {
     uint32_t x = static_cast<uint32_t>(i) + 0x9e3779b9u;
     x = (x ^ (x >> 16)) * 0x85ebca6bu;
     x = (x ^ (x >> 13)) * 0xc2b2ae35u;
     words += x ^ (x >> 16);
   }
+  // register loads (the reference's form) and bulk copies into shared memory
+  double ms_ldg = 0, ms_bulk = 0;
+  unsigned long long got = 0;
+  TRY(time_median([&] { return cmb_l2_read(buf.p, bytes, passes, 0, sum.as<unsigned long long>(), nullptr); },
+                  6, 1, &ms_ldg));
+  CMB_CUDA_TRY(cudaMemcpy(&got, sum.p, sizeof(got), cudaMemcpyDeviceToHost));
   if (got != words * passes)
     return fail(CMB_ERR_MISMATCH, "L2 read: word sum %llu != %llu", got, words * passes);
+  TRY(time_median([&] {
+        return cmb_l2_read_bulk(buf.p, bytes, passes, sum.as<unsigned long long>(), st.as<int>(), nullptr);
+      },
+      6, 1, &ms_bulk));
+  int status = 0;
+  CMB_CUDA_TRY(cudaMemcpy(&got, sum.p, sizeof(got), cudaMemcpyDeviceToHost));
+  CMB_CUDA_TRY(cudaMemcpy(&status, st.p, sizeof(status), cudaMemcpyDeviceToHost));
+  if (status != 0) return fail(status, "L2 bulk read: a bounded wait expired");
+  if (got != words * passes)
+    return fail(CMB_ERR_MISMATCH, "L2 bulk read: word sum %llu != %llu", got, words * passes);
   const double total = (double)bytes * passes;
-  printf("  L2 aggregate BW (%zu KiB resident, .cg 16-byte loads): %.2f GiB/s (%.1f GB/s)\n",
-         bytes >> 10, gib_per_s(total, ms), gb_per_s(total, ms));
+  const double ms = std::min(ms_ldg, ms_bulk);
+  printf("  L2 aggregate BW (%zu KiB resident): .cg 16-byte register loads %.1f GB/s, bulk "
+         "copies into shared memory %.1f GB/s\n",
+         bytes >> 10, gb_per_s(total, ms_ldg), gb_per_s(total, ms_bulk));
+  // the report's key carries the faster of the two reads of the same bytes
   g_results.log("memory_more", "l2_aggregate_bw_gibps", gib_per_s(total, ms), "GiB/s");
   g_results.log("memory_more", "l2_aggregate_bw_gbps", gb_per_s(total, ms), "GB/s");
+  g_results.log("memory_more", "l2_aggregate_ldg_bw_gbps", gb_per_s(total, ms_ldg), "GB/s");
+  g_results.log("memory_more", "l2_aggregate_bulk_bw_gbps", gb_per_s(total, ms_bulk), "GB/s");
   g_results.log("memory_more", "l2_aggregate_working_set_bytes", (double)bytes, "bytes");
   g_results.log("memory_more", "l2_aggregate_verified", 1.0, "bool");
   return CMB_OK;

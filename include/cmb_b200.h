@@ -128,6 +128,14 @@ size_t cmb_stream_sum_noalloc_max_ctas(void);
  * (src/memory_more.cu:66-85), whose float sum is replaced by an exact one. */
 int cmb_l2_read(const void *buf, size_t bytes, int passes, int ctas, unsigned long long *sum,
                 cmb_stream_t stream);
+/* The same exact sum with the bytes brought from L2 into shared memory by
+ * cp.async.bulk (the TMA unit): one CTA per SM, twelve warps each streaming
+ * 8 KiB chunks through a 2-stage ring (lane 0 loads, the warp adds the
+ * words).  bytes a positive multiple of 8 KiB; *status (device, may be
+ * NULL) = CMB_ERR_TIMEOUT if a chunk never landed within 2 s.  No reference
+ * counterpart (the reference reads L2 with register loads only). */
+int cmb_l2_read_bulk(const void *buf, size_t bytes, int passes, unsigned long long *sum,
+                     int *status, cmb_stream_t stream);
 
 /* Host-buffer stream copy: host_dst = host_src through the device.  Copies
  * chunks host->device, runs cmb_stream_copy on each, copies them back, with

@@ -198,3 +198,32 @@ def test_l2_read_exact_sum(cuda, cmb, orc, nbytes, passes, ctas):
     orc.orc_fill_hash_u32(ptr(ref), words)
     expect = (int(ref.astype(np.uint64).sum()) * passes) % (1 << 64)
     assert int(out.cpu().numpy().view(np.uint64)[0]) == expect
+
+
+@pytest.mark.parametrize("nbytes,passes", [(8192, 1), (8192 * 37, 3), (8 << 20, 16),
+                                           (64 << 20, 2)])
+def test_l2_read_bulk_exact_sum(cuda, cmb, orc, nbytes, passes):
+    """The bulk-copy L2 read: every 8 KiB chunk read `passes` times through
+    the shared-memory rings (fewer 8 KiB chunks than warps, a ragged share
+    per warp, and more than fit in L2), exact word sum against the oracle."""
+    words = nbytes // 4
+    d = cuda.empty(words, dtype=cuda.int32, device="cuda")
+    cmb.check("cmb_fill_hash_u32", dptr(d), words, stream_handle(cuda))
+    out = cuda.zeros(1, dtype=cuda.int64, device="cuda")
+    status = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    cmb.check("cmb_l2_read_bulk", dptr(d), nbytes, passes, dptr(out), dptr(status),
+              stream_handle(cuda))
+    ref = np.empty(words, np.uint32)
+    orc.orc_fill_hash_u32(ptr(ref), words)
+    expect = (int(ref.astype(np.uint64).sum()) * passes) % (1 << 64)
+    assert int(status.item()) == 0
+    assert int(out.cpu().numpy().view(np.uint64)[0]) == expect
+
+
+def test_l2_read_bulk_rejects_ragged_sizes(cuda, cmb):
+    d = cuda.zeros(1 << 16, dtype=cuda.int32, device="cuda")
+    out = cuda.zeros(1, dtype=cuda.int64, device="cuda")
+    s = stream_handle(cuda)
+    assert cmb.lib.cmb_l2_read_bulk(dptr(d), 8192 + 16, 1, dptr(out), None, s) == 1
+    assert cmb.lib.cmb_l2_read_bulk(dptr(d), 0, 1, dptr(out), None, s) == 1
+    assert cmb.lib.cmb_l2_read_bulk(dptr(d), 8192, 0, dptr(out), None, s) == 1
