@@ -5,13 +5,15 @@ The reference's main.cu declares and calls `void cmb::benchmark_<section>()`
 libcmb_b200.so must therefore export exactly the C ABI plus those section
 entry points, and keep its own results table private, so a reference build
 that links it has one g_results (its own) that the library logs into
-through cmb_results_set_sink().  No GPU call is made here."""
+through cmb_results_set_sink().  No GPU is needed (on a machine with one,
+the last test runs the global-memory section in a child process)."""
 
 import ctypes
 import os
 import re
 import shutil
 import subprocess
+import sys
 
 import pytest
 
@@ -92,3 +94,23 @@ def test_reference_executable_takes_probe_sections_from_library():
         assert re.search(rf" T cmb::benchmark_{s}\(\)$", local, re.M), s
     dyn = subprocess.run(["readelf", "-d", DROPIN], capture_output=True, text=True).stdout
     assert "libcmb_b200.so" in dyn and "$ORIGIN/../../cuda_micro_bench_b200/lib" in dyn
+
+
+def test_reference_entry_points_exit_like_the_reference(cmb):
+    """`void cmb::benchmark_global_memory()` keeps the reference's error
+    behaviour (CUDA_CHECK, include/utils.h:11-19): a failure prints the reason
+    and ends the process with EXIT_FAILURE.  Without a GPU the device query
+    fails; on a machine with a B200 the section runs and returns."""
+    script = (
+        "import ctypes, sys\n"
+        "lib = ctypes.CDLL(sys.argv[1])\n"
+        "getattr(lib, '_ZN3cmb23benchmark_global_memoryEv')()\n"
+        "print('returned')\n")
+    r = subprocess.run([sys.executable, "-c", script, cmb.library_path], capture_output=True,
+                       text=True, timeout=600)
+    if r.returncode == 0:
+        assert "returned" in r.stdout
+    else:
+        assert r.returncode == 1, (r.returncode, r.stderr)
+        assert "benchmark_global_memory failed: CMB_ERR_CUDA" in r.stderr, r.stderr
+        assert "returned" not in r.stdout
