@@ -216,7 +216,8 @@ def cpu_memcpy_baseline(sample_bytes: int, steps: int, warmup: int) -> dict:
 
 # Result flags of the probes: a check passed when its flag has this value.
 CHECK_FLAGS = {"bit_exact": True, "within_1e-2": True, "within_1e-5": True,
-               "endpoint_matches_host_walk": True, "landed_bytes_match": True, "status": 0}
+               "endpoint_matches_host_walk": True, "landed_bytes_match": True, "status": 0,
+               "bit_equal_to_plain_order": True}
 
 
 def failed_checks(node, path="") -> list:
@@ -548,18 +549,57 @@ def probe_tma(torch, stream, sh, peaks):
     return out
 
 
+def install_die_map(sh):
+    """Measures the die of every SM (cmb_sm_die_map) and installs the map
+    for the GEMMs (cmb_gemm_set_sm_die_map), which then run in the die-split
+    tile order.  Returns (labels or None, a summary for the JSON line)."""
+    import cuda_micro_bench_b200 as cmbpkg
+
+    t0 = time.perf_counter()
+    try:
+        labels, near, far = cmbpkg.sm_die_map(sh)
+    except cmbpkg.CmbError as e:
+        cmbpkg.set_sm_die_map(None)
+        return None, {"installed": False, "error": str(e)[:200]}
+    ms = (time.perf_counter() - t0) * 1e3
+    cmbpkg.set_sm_die_map(labels)
+    present = labels[labels != 0xFF]
+    return labels, {"installed": True, "sms_on_die": [int((present == d).sum()) for d in (0, 1)],
+                    "cold_load_cycles_near_far": [round(near), round(far)],
+                    "probe_ms": round(ms, 1)}
+
+
 def probe_gemm(torch, stream, sh, peaks):
     """Config: M=N=K=8192, A/B bf16 N(0,1)*K^-0.5, fp32 accumulation in
     TMEM, 2-CTA tiles of 256 x 512 (two N=256 accumulators per pair, held
     8-warp epilogue), and the 1-CTA 128x256 form; FP8 e4m3 with a per-tensor
-    scale.  TFLOP/s = 2*M*N*K / median launch time; every variant's output
-    is checked on 64 sampled 256x256 tiles (the two corner tiles included)
-    against an fp64 product of the same operands (max-norm per tile, rel
-    tol 1e-2).  cuBLAS (torch.mm /
+    scale.  The die map is measured and installed first, so the GEMMs run in
+    the die-split tile order; the 2-CTA fp32-C forms are also timed in the
+    plain order and their outputs compared bit for bit.  TFLOP/s = 2*M*N*K /
+    median launch time; every variant's output is checked on 64 sampled
+    256x256 tiles (the two corner tiles included) against an fp64 product of
+    the same operands (max-norm per tile, rel tol 1e-2).  cuBLAS (torch.mm /
     torch._scaled_mm) on the same operands with the same fp32 output is
     timed alongside as a live reference point; it is not part of the
     product."""
+    import cuda_micro_bench_b200 as cmbpkg
     from cuda_micro_bench_b200 import check
+
+    labels, die_summary = install_die_map(sh)
+
+    def plain_order(entry, fn, flop_):
+        """Times fn without the die map and compares its C with the die-split C."""
+        if labels is None:
+            return
+        split_c = C.clone()
+        cmbpkg.set_sm_die_map(None)
+        try:
+            ms_ = _median_ms(torch, stream, fn)
+            entry["bit_equal_to_plain_order"] = bool(torch.equal(C, split_c))
+        finally:
+            cmbpkg.set_sm_die_map(labels)
+        entry["plain_order_TFLOP/s"] = round(flop_ / (ms_ * 1e-3) / 1e12, 1)
+        del split_c
 
     M = N = K = 8192
     flop = 2.0 * M * N * K
@@ -601,7 +641,7 @@ def probe_gemm(torch, stream, sh, peaks):
 
     a64 = A.view(M, K).view(torch.bfloat16).double()
     b64 = B.view(N, K).view(torch.bfloat16).double()
-    out = {}
+    out = {"die_map": die_summary}
     for label, cg in (("bf16_8192_2cta", 2), ("bf16_8192_1cta", 1)):
         fn = lambda: check("cmb_gemm_bf16", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
                            ctypes.c_void_p(C.data_ptr()), M, N, K, cg,
@@ -613,6 +653,8 @@ def probe_gemm(torch, stream, sh, peaks):
                       "frac_of_2250_spec": round(tf / 2250.0, 4), "ms": round(ms, 4),
                       "sampled_tiles_max_rel_err": err, "within_1e-2": err <= 1e-2,
                       "status": int(status.item())}
+        if cg == 2:
+            plain_order(out[label], fn, flop)
     # the configuration's literal tile: 256 x 256 per 2-CTA pair (one N=256
     # MMA per K slice, two accumulators so the epilogue overlaps)
     fn = lambda: check("cmb_gemm_tuned", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
@@ -642,6 +684,8 @@ def probe_gemm(torch, stream, sh, peaks):
                       "frac_of_2x_measured_bf16": round(tf / (2 * peaks["bf16_tflops"]), 4),
                       "ms": round(ms, 4), "sampled_tiles_max_rel_err": err,
                       "within_1e-2": err <= 1e-2, "status": int(status.item())}
+        if cg == 2:
+            plain_order(out[label], fn, flop)
     # bf16 C (each fp32 accumulator rounded to nearest even), the output type
     # of the measured bf16 peak: cmb_gemm_bf16_out, 2-CTA held-epilogue tiles
     Cb = torch.empty(M * N, dtype=torch.bfloat16, device="cuda")
@@ -719,8 +763,17 @@ def probe_gemm(torch, stream, sh, peaks):
                           ("cublas_e4m3_bf16out", lambda: torch._scaled_mm(
                               f8a, f8b.t(), scale_a=sa[0], scale_b=sb[0], out_dtype=torch.bfloat16))):
             sustained[label] = _sustained(torch, stream, fn, flop, dev_index)
+        if labels is not None:  # ours again in the plain tile order
+            cmbpkg.set_sm_die_map(None)
+            try:
+                for label, fn in (("ours_bf16_bf16out_plain_order", ours_bf16),
+                                  ("ours_e4m3_bf16out_plain_order", ours_e4m3)):
+                    sustained[label] = _sustained(torch, stream, fn, flop, dev_index)
+            finally:
+                cmbpkg.set_sm_die_map(labels)
         sustained["what"] = ("each GEMM (8192^3, bf16 C) back to back for ~1 s with nvidia-smi "
-                             "sampling the SM clock every 5 ms")
+                             "sampling the SM clock every 5 ms; ours in the die-split tile order "
+                             "and, *_plain_order, without the die map")
     except (RuntimeError, TypeError) as e:
         sustained["error"] = str(e).splitlines()[0][:200]
     out["sustained_with_clocks"] = sustained
@@ -894,6 +947,40 @@ def probe_cublas(torch, stream, sh, ours_tile256=False) -> dict:
     return out
 
 
+def probe_gemm_die(torch, stream, sh) -> dict:
+    """The die-split tile order alone, for profiling it: the 8192^3 bf16
+    2-CTA GEMM (fp32 C) launched once to warm up and twice in the plain
+    order, then twice with the measured die map installed; the outputs
+    compared bit for bit."""
+    import cuda_micro_bench_b200 as cmbpkg
+    from cuda_micro_bench_b200 import check
+
+    M = N = K = 8192
+    A = torch.empty(M * K, dtype=torch.int16, device="cuda")
+    B = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(A.data_ptr()), M * K, ctypes.c_uint64(SEED + 1),
+          ctypes.c_float(K ** -0.5), sh)
+    check("cmb_fill_normal_bf16", ctypes.c_void_p(B.data_ptr()), N * K, ctypes.c_uint64(SEED + 2),
+          ctypes.c_float(K ** -0.5), sh)
+    C = torch.empty(M * N, dtype=torch.float32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    labels, out = install_die_map(sh)
+    fn = lambda: check("cmb_gemm_bf16", ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
+                       ctypes.c_void_p(C.data_ptr()), M, N, K, 2,
+                       ctypes.c_void_p(status.data_ptr()), sh)
+    cmbpkg.set_sm_die_map(None)
+    fn()  # warm-up: the first launch of the kernel in this process
+    ms = _time_launches(torch, stream, fn, 2)
+    plain = C.clone()
+    cmbpkg.set_sm_die_map(labels)
+    ms += _time_launches(torch, stream, fn, 2)
+    out["launch_ms_plain_plain_split_split"] = [round(x, 4) for x in ms]
+    out["bit_equal_to_plain_order"] = bool(torch.equal(C, plain))
+    out["status"] = int(status.item())
+    cmbpkg.set_sm_die_map(None)
+    return out
+
+
 def run_probe_only(args) -> int:
     """Runs only the named probes (for profiling) and prints their results."""
     import torch
@@ -916,6 +1003,8 @@ def run_probe_only(args) -> int:
             out["cublas_8192"] = probe_cublas(torch, stream, sh)
         elif name == "gemm256":
             out["gemm_256x256"] = probe_cublas(torch, stream, sh, ours_tile256=True)
+        elif name == "gemm_die":
+            out["gemm_die"] = probe_gemm_die(torch, stream, sh)
         torch.cuda.empty_cache()
     print(json.dumps({"probes": out}), flush=True)
     return 0
@@ -1026,7 +1115,7 @@ def main(argv=None) -> int:
     ap.add_argument("--quick-chase", action="store_true",
                     help="2^22 chase hops instead of the configuration's 2^24")
     ap.add_argument("--probe", action="append",
-                    choices=["stream", "chase", "tma", "gemm", "cublas", "gemm256"],
+                    choices=["stream", "chase", "tma", "gemm", "cublas", "gemm256", "gemm_die"],
                     help="run only this probe (repeatable); no headline line")
     args = ap.parse_args(argv)
     if args.warmup < 3:

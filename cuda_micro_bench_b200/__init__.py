@@ -6,7 +6,7 @@ CUDA for sm_100a behind the C ABI of ``include/cmb_b200.h``) and the C++ CLI
 it (``build``); there is no Python or CPU fallback for any probe.
 """
 
-__all__ = ["CmbError", "lib", "check", "library_path"]
+__all__ = ["CmbError", "lib", "check", "library_path", "sm_die_map", "set_sm_die_map"]
 
 
 def __getattr__(name):

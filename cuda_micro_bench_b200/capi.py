@@ -51,6 +51,8 @@ SIGNATURES = {
     "cmb_gemm_e4m3": (_i, [_p, _p, _p, _i, _i, _i, _p, _p, _i, _p, _p]),
     "cmb_gemm_tuned": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
     "cmb_gemm_bf16_out": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p]),
+    "cmb_sm_die_map": (_i, [_p, _i, _p, _p, _p]),
+    "cmb_gemm_set_sm_die_map": (_i, [_p, _i]),
     "cmb_mma_rate": (_i, [_i, _i, _i, _p, _p, _p, _p]),
     "cmb_quantize_e4m3": (_i, [_p, _sz, _p, _p, _p]),
     "cmb_mma_sync_latency": (_i, [_i, _i, _p, _p, _p]),
@@ -112,3 +114,29 @@ def check(fn: str, *args) -> int:
     if rc != 0:
         raise CmbError(fn, rc)
     return rc
+
+
+def sm_die_map(stream=None):
+    """Measures the die of every SM of the current device (cmb_sm_die_map).
+    Returns (labels, near_cycles, far_cycles): labels[id] is 0 or 1 for each
+    SM id, 0xFF for ids without an SM (a uint8 numpy array)."""
+    import numpy as np
+
+    labels = np.full(256, 0xFF, np.uint8)
+    n_ids = ctypes.c_int(0)
+    near_far = (ctypes.c_float * 2)()
+    check("cmb_sm_die_map", ctypes.c_void_p(labels.ctypes.data), len(labels), ctypes.byref(n_ids),
+          near_far, stream)
+    return labels[:n_ids.value].copy(), float(near_far[0]), float(near_far[1])
+
+
+def set_sm_die_map(labels):
+    """Installs `labels` (as sm_die_map returns them) for the GEMMs on the
+    current device; None removes the map (cmb_gemm_set_sm_die_map)."""
+    import numpy as np
+
+    if labels is None:
+        check("cmb_gemm_set_sm_die_map", None, 0)
+        return
+    a = np.ascontiguousarray(labels, dtype=np.uint8)
+    check("cmb_gemm_set_sm_die_map", ctypes.c_void_p(a.ctypes.data), len(a))

@@ -29,6 +29,9 @@ uint64_t splitmix64_host(uint64_t seed, uint64_t i);
 // (cmb_device_reset calls these before resetting the device).
 void p2p_release_streams(int dev);
 void host_copy_release_streams(int dev);
+// Forget the die map installed for device `dev` (its device copy is gone
+// after a reset).
+void gemm_release_die_map(int dev);
 
 // The source file's name without its directories (error messages name the
 // file, not the machine it was built on).

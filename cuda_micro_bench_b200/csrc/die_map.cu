@@ -1,0 +1,215 @@
+// die_map.cu — which of the B200's two dies each SM sits on, measured.
+//
+// A B200 is two dies joined by a die-to-die link; device memory is
+// interleaved across the HBM stacks of both, so every cache line is homed on
+// one die.  A load that misses L2 costs one die crossing more when the line
+// is homed on the other die (on B200: ~1000 against ~610 cycles).  So for a
+// fixed set of lines, SMs on the same die see the same near/far pattern, and
+// the two dies see complementary ones.
+//
+// The probe, once per SM: evict L2 by writing a 256 MiB buffer, then let the
+// CTA that runs on the SM under test time dependent loads of kLines lines of
+// a separate, never-written region (every other CTA of the launch only
+// stays resident long enough that each SM holds exactly one CTA).  The host
+// splits the SMs by their pattern and checks that the split is clean.  The
+// map feeds the GEMM's die-split tile order (cmb_gemm_set_sm_die_map); it
+// differs between B200s (which SMs are fused off varies per part), so it is
+// measured on the device that uses it.
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "cmb_device.cuh"
+#include "cmb_host.h"
+
+namespace cmb {
+namespace {
+
+constexpr int kLines = 96;                          // probed lines
+constexpr size_t kFlushBytes = 256ull << 20;         // > 2 x the 126 MB L2
+constexpr size_t kRegionBytes = 32ull << 20;         // the probed lines live here
+constexpr size_t kRegionLines = kRegionBytes / 128;
+constexpr int kProbeSmem = 120 * 1024;               // > half an SM: one CTA per SM
+constexpr uint64_t kDwellNs = 100000;                // residency of every CTA
+constexpr int kReps = 2;                             // the last repetition is kept
+
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void dwell_from(uint64_t t0) {
+  while (dev::globaltimer() - t0 < kDwellNs) {
+  }
+}
+
+// present[id] = 1 for the %smid of every SM that runs a CTA; ids at or
+// above CMB_DIE_MAP_IDS set present[CMB_DIE_MAP_IDS].
+__global__ void k_die_present(int *present) {
+  extern __shared__ uint8_t pad[];
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = dev::globaltimer();
+  const uint32_t id = smid();
+  present[id < CMB_DIE_MAP_IDS ? id : CMB_DIE_MAP_IDS] = 1;
+  if (pad[0] == 0xA5 && id == 0xFFFFFFFFu) present[0] = 2;  // keeps the shared-memory request
+  dwell_from(t0);
+}
+
+// The CTA on SM `target` times one dependent load of each line; the loaded
+// value (the region is zero) only adds 0 or 1 words to the next address, so
+// every load stays inside the region.
+__global__ void k_die_probe(const uint32_t *region, const uint32_t *lines, int target,
+                            uint32_t *lat, int *found) {
+  extern __shared__ uint8_t pad[];
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = dev::globaltimer();
+  if (smid() == static_cast<uint32_t>(target)) {
+    atomicAdd(found, 1);
+    uint32_t v = 0;
+    for (int j = 0; j < kLines; ++j) {
+      const uint32_t *p = region + static_cast<size_t>(lines[j]) * 32 + (v != 0 ? 1 : 0);
+      const uint64_t c0 = dev::clock64_after(v);
+      const uint32_t x = dev::ld_cg_u32(p);
+      const uint64_t c1 = dev::clock64_after(x);
+      v = x;
+      lat[j] = static_cast<uint32_t>(c1 - c0);
+    }
+    if (pad[0] == 0xA5 && v == 0xFFFFFFFFu) lat[0] = 0;  // keeps the shared-memory request
+  }
+  dwell_from(t0);
+}
+
+double median(std::vector<double> v) {
+  if (v.empty()) return 0.0;
+  const size_t m = v.size() / 2;
+  std::nth_element(v.begin(), v.begin() + static_cast<long>(m), v.end());
+  return v[m];
+}
+
+struct Scratch {
+  uint8_t *base = nullptr;
+  ~Scratch() {
+    if (base != nullptr) cudaFree(base);
+  }
+};
+
+}  // namespace
+}  // namespace cmb
+
+using namespace cmb;
+
+extern "C" int cmb_sm_die_map(uint8_t *sm_die, int capacity, int *n_ids, float *near_far_cycles,
+                              cmb_stream_t stream) {
+  if (sm_die == nullptr || n_ids == nullptr)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_sm_die_map: null output");
+  if (capacity <= 0) return fail(CMB_ERR_INVALID_ARG, "cmb_sm_die_map: capacity %d", capacity);
+  const int nsm = current_sm_count();
+  if (nsm <= 0) return fail(CMB_ERR_CUDA, "cmb_sm_die_map: no current device");
+
+  // one allocation: flush buffer, probed region, line list, results
+  const size_t lines_off = kFlushBytes + kRegionBytes;
+  const size_t present_off = lines_off + kLines * sizeof(uint32_t);
+  const size_t found_off = present_off + (CMB_DIE_MAP_IDS + 1) * sizeof(int);
+  const size_t lat_off = found_off + CMB_DIE_MAP_IDS * sizeof(int);
+  const size_t total = lat_off + static_cast<size_t>(CMB_DIE_MAP_IDS) * kLines * sizeof(uint32_t);
+  Scratch s;
+  CMB_CUDA_TRY(cudaMalloc(&s.base, total));
+  uint8_t *flush = s.base;
+  auto *region = reinterpret_cast<uint32_t *>(s.base + kFlushBytes);
+  auto *lines_d = reinterpret_cast<uint32_t *>(s.base + lines_off);
+  auto *present_d = reinterpret_cast<int *>(s.base + present_off);
+  auto *found_d = reinterpret_cast<int *>(s.base + found_off);
+  auto *lat_d = reinterpret_cast<uint32_t *>(s.base + lat_off);
+
+  std::vector<uint32_t> lines(kLines);
+  for (int j = 0; j < kLines; ++j)  // spread over the region; the last line is never used
+    lines[j] = static_cast<uint32_t>(splitmix64_host(0xD1Eull, static_cast<uint64_t>(j)) %
+                                     (kRegionLines - 1));
+  CMB_CUDA_TRY(cudaMemsetAsync(region, 0, kRegionBytes, stream));
+  CMB_CUDA_TRY(cudaMemsetAsync(present_d, 0, lat_off - present_off, stream));
+  CMB_CUDA_TRY(cudaMemcpyAsync(lines_d, lines.data(), kLines * sizeof(uint32_t),
+                               cudaMemcpyHostToDevice, stream));
+  CMB_CUDA_TRY(cudaFuncSetAttribute(k_die_present, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kProbeSmem));
+  CMB_CUDA_TRY(cudaFuncSetAttribute(k_die_probe, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kProbeSmem));
+  k_die_present<<<nsm, 32, kProbeSmem, stream>>>(present_d);
+  CMB_LAUNCH_CHECK();
+  std::vector<int> present(CMB_DIE_MAP_IDS + 1);
+  CMB_CUDA_TRY(cudaMemcpyAsync(present.data(), present_d, present.size() * sizeof(int),
+                               cudaMemcpyDeviceToHost, stream));
+  CMB_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (present[CMB_DIE_MAP_IDS] != 0)
+    return fail(CMB_ERR_UNSUPPORTED, "cmb_sm_die_map: an SM id is %d or more", CMB_DIE_MAP_IDS);
+  std::vector<int> ids;
+  for (int i = 0; i < CMB_DIE_MAP_IDS; ++i)
+    if (present[i] != 0) ids.push_back(i);
+  if (static_cast<int>(ids.size()) != nsm)
+    return fail(CMB_ERR_MISMATCH, "cmb_sm_die_map: %zu of %d SMs ran a CTA", ids.size(), nsm);
+  const int id_end = ids.back() + 1;
+  if (id_end > capacity)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_sm_die_map: capacity %d below %d SM ids", capacity,
+                id_end);
+
+  for (int rep = 0; rep < kReps; ++rep) {
+    for (int t : ids) {
+      CMB_CUDA_TRY(cudaMemsetAsync(flush, (rep * 31 + t) & 0xFF, kFlushBytes, stream));
+      k_die_probe<<<nsm, 32, kProbeSmem, stream>>>(region, lines_d, t,
+                                                   lat_d + static_cast<size_t>(t) * kLines,
+                                                   found_d + t);
+      CMB_LAUNCH_CHECK();
+    }
+  }
+  std::vector<int> found(CMB_DIE_MAP_IDS);
+  std::vector<uint32_t> lat(static_cast<size_t>(CMB_DIE_MAP_IDS) * kLines);
+  CMB_CUDA_TRY(cudaMemcpyAsync(found.data(), found_d, found.size() * sizeof(int),
+                               cudaMemcpyDeviceToHost, stream));
+  CMB_CUDA_TRY(cudaMemcpyAsync(lat.data(), lat_d, lat.size() * sizeof(uint32_t),
+                               cudaMemcpyDeviceToHost, stream));
+  CMB_CUDA_TRY(cudaStreamSynchronize(stream));
+  for (int t : ids)
+    if (found[t] != kReps)
+      return fail(CMB_ERR_MISMATCH, "cmb_sm_die_map: SM %d ran the probe %d times, not %d", t,
+                  found[t], kReps);
+
+  // per line: far (1) when slower than the median over SMs
+  const size_t n = ids.size();
+  std::vector<std::vector<uint8_t>> far(n, std::vector<uint8_t>(kLines));
+  std::vector<double> near_lat, far_lat;
+  for (int j = 0; j < kLines; ++j) {
+    std::vector<double> col(n);
+    for (size_t i = 0; i < n; ++i) col[i] = lat[static_cast<size_t>(ids[i]) * kLines + j];
+    const double m = median(col);
+    for (size_t i = 0; i < n; ++i) {
+      far[i][j] = col[i] > m ? 1 : 0;
+      (far[i][j] ? far_lat : near_lat).push_back(col[i]);
+    }
+  }
+  // die 0 = the SMs whose pattern agrees with the lowest SM id's
+  std::vector<uint8_t> die(n);
+  int count[2] = {0, 0};
+  double worst = 0.0;
+  for (size_t i = 0; i < n; ++i) {
+    int same = 0;
+    for (int j = 0; j < kLines; ++j) same += far[i][j] == far[0][j];
+    const double agree = static_cast<double>(same) / kLines;
+    die[i] = agree > 0.5 ? 0 : 1;
+    ++count[die[i]];
+    worst = std::max(worst, std::min(agree, 1.0 - agree));
+  }
+  const double near_med = median(near_lat), far_med = median(far_lat);
+  if (near_far_cycles != nullptr) {
+    near_far_cycles[0] = static_cast<float>(near_med);
+    near_far_cycles[1] = static_cast<float>(far_med);
+  }
+  if (count[0] == 0 || count[1] == 0 || worst > 0.35 || far_med - near_med < 100.0)
+    return fail(CMB_ERR_MISMATCH,
+                "cmb_sm_die_map: no clean two-die split (%d / %d SMs, worst pattern agreement "
+                "%.2f, near %.0f / far %.0f cycles)",
+                count[0], count[1], 1.0 - worst, near_med, far_med);
+  for (int i = 0; i < capacity; ++i) sm_die[i] = 0xFF;
+  for (size_t i = 0; i < n; ++i) sm_die[ids[i]] = die[i];
+  *n_ids = id_end;
+  return CMB_OK;
+}

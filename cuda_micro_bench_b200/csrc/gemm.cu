@@ -34,11 +34,25 @@
 //   into registers and hands that half back before storing it, and the MMA
 //   issuer starts the next tile on half 0 over the stages already loaded
 //   while half 1 drains ("held" epilogue).
+// Tile order: persistent clusters walk the tiles in raster groups of group_m
+// tile rows.  With a die map installed (cmb_gemm_set_sm_die_map) the tiles
+// are cut into two contiguous ranges, one per die of the B200 in proportion
+// to its SMs, and each cluster works in the range of the die it runs on, so
+// the operand lines one die reads are less often also read by the other die
+// (fewer die-to-die crossings and L2 reads).  A cluster claims a slot of its
+// die's range with an atomic counter, or a slot of the other range when its
+// own are taken; there are as many slots as clusters, so every tile is
+// computed once whatever the map says or where the clusters land.  The last
+// cluster to claim resets the counters for the next launch.
 // All waits are bounded; a wait that gives up reports CMB_ERR_TIMEOUT in
 // `status` and every role drains and leaves.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
+
+#include <atomic>
+#include <cmath>
+#include <mutex>
 
 #include "cmb_device.cuh"
 #include "cmb_host.h"
@@ -49,6 +63,15 @@ namespace cmb {
 int make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t rows,
                  uint64_t cols, uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols,
                  CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo);
+
+// Die (0 or 1) of the SM with each %smid on this device, written by
+// cmb_gemm_set_sm_die_map.  Every device holds its own copy.
+__device__ uint8_t g_sm_die[CMB_DIE_MAP_IDS];
+// Slot-claim counters of the die-split tile order: per launch slot, claims
+// made on die 0 and die 1 and the number of clusters done claiming.  Zero
+// between launches.
+constexpr int kClaimSlots = 64;
+__device__ unsigned g_tile_claims[kClaimSlots][4];
 
 namespace {
 
@@ -122,7 +145,8 @@ template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW, bool 
 __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
            const __grid_constant__ CUtensorMap tmC, void *__restrict__ Cv, int M, int N, int K,
-           const float *scale_a, const float *scale_b, int group_m, int *status) {
+           const float *scale_a, const float *scale_b, int group_m, int die_pairs0,
+           int claim_slot, int *status) {
   using Cfg = GemmCfg<CG, kFp8, STAGES, kTmaEpi, NSUB, EPIW>;
   static_assert(!kBf16Out || Cfg::kHeld, "bf16 output needs the held epilogue");
   float *const C = static_cast<float *>(Cv);
@@ -158,16 +182,63 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     tc::tmem_alloc<CG>(dev::smem_addr(&tmem_holder), Cfg::kTmemCols);
     tc::tmem_relinquish<CG>();
   }
+  const int tiles_m = (M + Cfg::kTileM - 1) / Cfg::kTileM;
+  const int tiles_n = (N + Cfg::kTileN - 1) / Cfg::kTileN;
+  const int tiles = tiles_m * tiles_n;
+  // This cluster's tiles: t_first, t_first + t_step, ... below t_end.  CTA 0
+  // decides and writes the three numbers into both CTAs' shared memory
+  // before the cluster barrier below.
+  __shared__ int tile_seq[3];
+  if (threadIdx.x == 0 && rank == 0) {
+    const int nclusters = gridDim.x / CG;
+    int first = blockIdx.x / CG, step = nclusters, end = tiles;
+    if (die_pairs0 >= 0) {
+      uint32_t sm;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+      const int pairs[2] = {die_pairs0, nclusters - die_pairs0};
+      unsigned *claims = g_tile_claims[claim_slot];
+      int d = sm < CMB_DIE_MAP_IDS ? (g_sm_die[sm] & 1) : 0;
+      int slot = static_cast<int>(atomicAdd(&claims[d], 1u));
+      if (slot >= pairs[d]) {
+        d ^= 1;
+        slot = static_cast<int>(atomicAdd(&claims[d], 1u));
+      }
+      __threadfence();
+      if (atomicAdd(&claims[2], 1u) == static_cast<unsigned>(nclusters - 1)) {
+        // every cluster has claimed: leave the counters at zero
+        __threadfence();
+        atomicExch(&claims[0], 0u);
+        atomicExch(&claims[1], 0u);
+        atomicExch(&claims[2], 0u);
+      }
+      const int split = static_cast<int>(static_cast<long long>(tiles) * pairs[0] / nclusters);
+      if (slot < pairs[d]) {
+        first = (d == 0 ? 0 : split) + slot;
+        step = pairs[d];
+        end = d == 0 ? split : tiles;
+      } else {  // no slot left: only if the counters were not at zero
+        dev::report_status(status, CMB_ERR_MISMATCH);
+        first = tiles;
+      }
+    }
+    tile_seq[0] = first;
+    tile_seq[1] = step;
+    tile_seq[2] = end;
+    if constexpr (CG == 2) {
+      const int v[3] = {first, step, end};
+      for (int i = 0; i < 3; ++i)
+        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(
+                         tc::map_to_cta(dev::smem_addr(&tile_seq[i]), 1)),
+                     "r"(v[i])
+                     : "memory");
+    }
+  }
   tc::fence_before_sync();
   if constexpr (CG == 2) tc::cluster_sync();
   else __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem_base = tmem_holder;
-
-  const int tiles_m = (M + Cfg::kTileM - 1) / Cfg::kTileM;
-  const int tiles_n = (N + Cfg::kTileN - 1) / Cfg::kTileN;
-  const int tiles = tiles_m * tiles_n;
-  const int cluster = blockIdx.x / CG, nclusters = gridDim.x / CG;
+  const int t_first = tile_seq[0], t_step = tile_seq[1], t_end = tile_seq[2];
   const int kblocks = (K + Cfg::kBk - 1) / Cfg::kBk;
 
   if (warp == 0) {
@@ -175,7 +246,7 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
       // ---------------------------------------------------------- producer
       int it = 0;
       bool ok = true;
-      for (int t = cluster; t < tiles && ok; t += nclusters) {
+      for (int t = t_first; t < t_end && ok; t += t_step) {
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
         const int a_row = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kBmCta;
@@ -226,7 +297,7 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
       int it = 0, j = 0;
       bool ok = true;
       const int pre = kblocks < Cfg::kStages ? kblocks : Cfg::kStages;
-      for (int t = cluster; t < tiles && ok; t += nclusters, ++j) {
+      for (int t = t_first; t < t_end && ok; t += t_step, ++j) {
         const uint32_t aph = static_cast<uint32_t>(j) & 1;
         for (int u = 0; u < 2 && ok; ++u) {
           if (!dev::mbar_wait_bounded(dev::smem_addr(&tempty[u]), aph ^ 1) ||
@@ -301,7 +372,7 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
       // --------------------------------------------------------- MMA issuer
       int it = 0, j = 0;
       bool ok = true;
-      for (int t = cluster; t < tiles && ok; t += nclusters, ++j) {
+      for (int t = t_first; t < t_end && ok; t += t_step, ++j) {
         const int a = j % Cfg::kAccBufs;
         const uint32_t aph = (j / Cfg::kAccBufs) & 1;
         if (!dev::mbar_wait_bounded(dev::smem_addr(&tempty[a]), aph ^ 1)) {
@@ -362,7 +433,7 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     uint8_t *box = ring + (size_t)Cfg::kStages * Cfg::kStageBytes + (size_t)ew * Cfg::kEpiBoxBytes;
     uint32_t epi_count = 0;
     int j = 0;
-    for (int t = cluster; t < tiles; t += nclusters, ++j) {
+    for (int t = t_first; t < t_end; t += t_step, ++j) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
       if (!dev::mbar_wait_bounded(dev::smem_addr(&tfull[0]), static_cast<uint32_t>(j) & 1) ||
@@ -513,7 +584,7 @@ __global__ void __launch_bounds__(64 + 32 * EPIW, 1)
     uint8_t *epi = ring + (size_t)Cfg::kStages * Cfg::kStageBytes + (size_t)ew * 2 * Cfg::kEpiBoxBytes;
     uint32_t epi_count = 0;
     int j = 0;
-    for (int t = cluster; t < tiles; t += nclusters, ++j) {
+    for (int t = t_first; t < t_end; t += t_step, ++j) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, group_m, tm, tn);
       const int a = j % Cfg::kAccBufs;
@@ -634,6 +705,35 @@ __global__ void k_quantize_e4m3(const __nv_bfloat16 *__restrict__ x, size_t n,
     scale_out[0] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
 }
 
+// Installed die maps, per device: SMs on each die (0 / 0 = none installed).
+constexpr int kMaxDevices = 64;
+std::mutex g_die_mu;
+int g_die_sms[kMaxDevices][2];
+std::atomic<unsigned> g_claim_seq{0};
+
+// Clusters that work in die 0's tile range (the rest work in die 1's), or
+// -1 for the plain order when no map is installed on the current device;
+// `slot` = the claim counters this launch uses.
+void die_split(int cg, int clusters, int *pairs0, int *slot) {
+  *pairs0 = -1;
+  *slot = 0;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  int sms[2];
+  {
+    std::lock_guard<std::mutex> lk(g_die_mu);
+    sms[0] = g_die_sms[dev][0];
+    sms[1] = g_die_sms[dev][1];
+  }
+  const int cap0 = sms[0] / cg, cap1 = sms[1] / cg;
+  if (cap0 + cap1 <= 0) return;
+  long p0 = std::lround(static_cast<double>(clusters) * cap0 / (cap0 + cap1));
+  if (p0 < 0) p0 = 0;
+  if (p0 > clusters) p0 = clusters;
+  *pairs0 = static_cast<int>(p0);
+  *slot = static_cast<int>(g_claim_seq.fetch_add(1u, std::memory_order_relaxed) % kClaimSlots);
+}
+
 template <int CG, bool kFp8, int STAGES, bool kTmaEpi, int NSUB, int EPIW, bool kBf16Out = false>
 int launch_gemm(const void *A, const void *B, void *C, int M, int N, int K,
                 const float *scale_a, const float *scale_b, int group_m, int *status,
@@ -679,8 +779,10 @@ int launch_gemm(const void *A, const void *B, void *C, int M, int N, int K,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  int die_pairs0, claim_slot;
+  die_split(CG, clusters, &die_pairs0, &claim_slot);
   CMB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, C, M, N, K, scale_a, scale_b,
-                                  group_m, status));
+                                  group_m, die_pairs0, claim_slot, status));
   return CMB_OK;
 }
 
@@ -817,6 +919,45 @@ extern "C" int cmb_gemm_bf16_out(const void *A, const void *B, void *C, int M, i
                                                              status, stream)
                 : launch_gemm<2, false, 4, false, 2, 8, true>(A, B, C, M, N, K, nullptr, nullptr, 8,
                                                               status, stream);
+}
+
+namespace cmb {
+void gemm_release_die_map(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lk(g_die_mu);
+  g_die_sms[dev][0] = g_die_sms[dev][1] = 0;
+}
+}  // namespace cmb
+
+extern "C" int cmb_gemm_set_sm_die_map(const uint8_t *sm_die, int n_ids) {
+  int count[2] = {0, 0};
+  uint8_t map[CMB_DIE_MAP_IDS] = {0};
+  const bool clear = sm_die == nullptr || n_ids == 0;
+  if (!clear) {
+    if (n_ids < 0 || n_ids > CMB_DIE_MAP_IDS)
+      return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_set_sm_die_map: %d ids, not 1-%d", n_ids,
+                  CMB_DIE_MAP_IDS);
+    for (int i = 0; i < n_ids; ++i) {
+      if (sm_die[i] == 0xFF) continue;  // no SM with this id
+      if (sm_die[i] > 1)
+        return fail(CMB_ERR_INVALID_ARG, "cmb_gemm_set_sm_die_map: SM %d on die %d, not 0 or 1",
+                    i, sm_die[i]);
+      map[i] = sm_die[i];
+      ++count[sm_die[i]];
+    }
+    if (count[0] == 0 || count[1] == 0)
+      return fail(CMB_ERR_INVALID_ARG,
+                  "cmb_gemm_set_sm_die_map: both dies need SMs (%d / %d)", count[0], count[1]);
+  }
+  int dev = -1;
+  CMB_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(CMB_ERR_UNSUPPORTED, "cmb_gemm_set_sm_die_map: device %d", dev);
+  if (!clear) CMB_CUDA_TRY(cudaMemcpyToSymbol(g_sm_die, map, sizeof(map)));
+  std::lock_guard<std::mutex> lk(g_die_mu);
+  g_die_sms[dev][0] = count[0];
+  g_die_sms[dev][1] = count[1];
+  return CMB_OK;
 }
 
 extern "C" int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst,

@@ -68,6 +68,7 @@ extern "C" int cmb_device_reset(void) {
   CMB_CUDA_TRY(cudaGetDevice(&dev));
   cmb::p2p_release_streams(dev);
   cmb::host_copy_release_streams(dev);
+  cmb::gemm_release_die_map(dev);
   CMB_CUDA_TRY(cudaDeviceReset());
   return CMB_OK;
 }

@@ -151,12 +151,22 @@ def check(doc, full=True, keys=None):
                     ("fp8_e4m3_gemm_8192", B200["fp8_tflops"])):
         bound("tensor_core_tcgen05", p + "_tflops", 0, spec * 1.05, "dense tensor peak")
         bound("tensor_core_tcgen05", p + "_bf16out_tflops", 0, spec * 1.05, "dense tensor peak")
+        bound("tensor_core_tcgen05", p + "_plain_order_tflops", 0, spec * 1.05, "dense tensor peak")
         flag("tensor_core_tcgen05", p + "_verified")
         flag("tensor_core_tcgen05", p + "_bf16out_verified")
         err = val("tensor_core_tcgen05", p + "_max_rel_err")
         if err is not None and err > 1e-2:
             fail(f"tensor_core_tcgen05.{p}_max_rel_err = {err} above 1e-2")
     bound("peak", "fp16_tensor_tflops", 0, B200["bf16_tflops"] * 1.05, "dense fp16 tensor peak")
+    # the die map: every SM on one of two dies, far loads slower than near
+    dies = [val("tensor_core_tcgen05", f"sms_on_die{d}") for d in (0, 1)]
+    if all(x is not None for x in dies) and (min(dies) <= 0 or sum(dies) != B200["sm_count"]):
+        fail(f"tensor_core_tcgen05.sms_on_die0/1 = {dies[0]} / {dies[1]}: not a split of "
+             f"{B200['sm_count']} SMs")
+    near = val("tensor_core_tcgen05", "die_near_load_latency_cyc")
+    far = val("tensor_core_tcgen05", "die_far_load_latency_cyc")
+    if near is not None and far is not None and not (0 < near < far):
+        fail(f"tensor_core_tcgen05 die load latency near {near} / far {far} cycles")
 
     # host link and NVLink
     for k in ("htod_bandwidth_GiB_s", "dtoh_bandwidth_GiB_s"):

@@ -272,6 +272,36 @@ int cmb_mma_rate(int fp8, int iters, int ctas, float *out, uint64_t *cycles, int
 int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst, float *scale_out,
                       cmb_stream_t stream);
 
+/* --- die-aware tile order for the GEMMs (no reference counterpart: the
+ *     reference's tensor probes read no memory) ---------------------------- */
+
+/* Size of a per-SM die map: one entry per %smid value. */
+#define CMB_DIE_MAP_IDS 256
+/* Measures which of the B200's two dies each SM of the current device sits
+ * on: after L2 is evicted, each SM in turn times cold loads of the same 96
+ * lines; a line homed on the other die's memory takes a die crossing more,
+ * so SMs of one die share a near/far pattern.  sm_die[id] (host, capacity
+ * entries) = 0 or 1 for every SM id (die 0 holds the lowest id), 0xFF for
+ * ids no SM has; *n_ids = highest SM id + 1.  near_far_cycles (host, 2
+ * floats, may be NULL) = median cold-load latency near and far.  Runs ~300
+ * short launches on `stream` (tens of ms), allocates and frees 288 MiB of
+ * device memory, and needs the device otherwise idle (every SM must take
+ * one of its CTAs).  CMB_ERR_MISMATCH when the SMs do not split cleanly in
+ * two. */
+int cmb_sm_die_map(uint8_t *sm_die, int capacity, int *n_ids, float *near_far_cycles,
+                   cmb_stream_t stream);
+/* Installs a die map (as cmb_sm_die_map returns it: n_ids entries of 0, 1
+ * or 0xFF, both dies non-empty) for the GEMMs that later launch on the
+ * current device: their tiles are cut into one contiguous range per die,
+ * in proportion to its SMs, and each CTA cluster works in its own die's
+ * range, so less operand data crosses between the dies.  The result is
+ * bit-identical with or without a map, and with any map: the map only moves
+ * tiles between clusters.  sm_die == NULL or n_ids == 0 removes the map
+ * (the plain persistent order).  Copies the map to the device
+ * synchronously: call it while no GEMM of this library runs on the device.
+ * Up to 64 GEMM launches may run on one device at the same time. */
+int cmb_gemm_set_sm_die_map(const uint8_t *sm_die, int n_ids);
+
 /* --- legacy warp-level mma.sync probes (src/tensor_core.cu,
  *     src/tensor_core_extended.cu) ------------------------------------- */
 

@@ -143,3 +143,26 @@ def test_cli_usage_and_unknown_flag(tmp_path):
     p = subprocess.run([exe, "--bogus", f"--out={out}"], capture_output=True, text=True)
     assert p.returncode == 1 and "Unknown option: --bogus" in p.stdout
     assert not out.exists()
+
+
+def test_die_map_entry_points_reject_bad_arguments(cmb):
+    """Argument checks that come before any device call (no GPU needed)."""
+
+    def rc(fn, *args):
+        return getattr(cmb.lib, fn)(*args)
+
+    p = lambda a: ctypes.c_void_p(a.ctypes.data)
+    two_dies = np.array([0, 0, 1, 1, 0xFF, 1], np.uint8)
+    assert rc("cmb_gemm_set_sm_die_map", p(two_dies), 300) == 1  # more ids than a map holds
+    assert rc("cmb_gemm_set_sm_die_map", p(two_dies), -1) == 1
+    bad_label = np.array([0, 1, 2, 1], np.uint8)
+    assert rc("cmb_gemm_set_sm_die_map", p(bad_label), 4) == 1
+    assert "not 0 or 1" in cmb.lib.cmb_last_error().decode()
+    one_die = np.array([0, 0, 0xFF, 0], np.uint8)
+    assert rc("cmb_gemm_set_sm_die_map", p(one_die), 4) == 1
+    assert "both dies" in cmb.lib.cmb_last_error().decode()
+    out = np.zeros(256, np.uint8)
+    n = ctypes.c_int(0)
+    assert rc("cmb_sm_die_map", None, 256, ctypes.byref(n), None, None) == 1
+    assert rc("cmb_sm_die_map", p(out), 256, None, None, None) == 1
+    assert rc("cmb_sm_die_map", p(out), 0, ctypes.byref(n), None, None) == 1

@@ -55,6 +55,11 @@ MEASURED = [
     ("tma", "tile_copy_bw_gbps", 6100.0, "GB/s"),
     ("tma", "tile_copy_verified", 1.0, "bool"),
     ("tensor_core_tcgen05", "bf16_gemm_8192_tflops", 1519.0, "TFLOP/s"),
+    ("tensor_core_tcgen05", "bf16_gemm_8192_plain_order_tflops", 1501.0, "TFLOP/s"),
+    ("tensor_core_tcgen05", "sms_on_die0", 70.0, "count"),
+    ("tensor_core_tcgen05", "sms_on_die1", 78.0, "count"),
+    ("tensor_core_tcgen05", "die_near_load_latency_cyc", 610.0, "cycles"),
+    ("tensor_core_tcgen05", "die_far_load_latency_cyc", 1000.0, "cycles"),
     ("tensor_core_tcgen05", "bf16_gemm_8192_verified", 1.0, "bool"),
     ("tensor_core_tcgen05", "bf16_gemm_8192_max_rel_err", 1.2e-5, ""),
     ("tensor_core_tcgen05", "fp8_e4m3_gemm_8192_tflops", 2789.0, "TFLOP/s"),
@@ -110,6 +115,9 @@ def _set(doc, sec, key, value, unit=None):
     ("tma", "tile_copy_verified", 0.0, None, "output check failed"),
     ("tensor_core_tcgen05", "bf16_gemm_8192_tflops", 2500.0, None, "dense tensor peak"),
     ("tensor_core_tcgen05", "fp8_e4m3_gemm_8192_max_rel_err", 0.05, None, "above 1e-2"),
+    ("tensor_core_tcgen05", "bf16_gemm_8192_plain_order_tflops", 2600.0, None, "dense tensor peak"),
+    ("tensor_core_tcgen05", "sms_on_die1", 70.0, None, "not a split of"),
+    ("tensor_core_tcgen05", "die_far_load_latency_cyc", 500.0, None, "die load latency"),
     ("p2p", "ring_store_link_gbps", 1000.0, None, "NVLink 5"),
     ("pcie", "htod_bandwidth_GiB_s", 80.0, None, "PCIe Gen5"),
     ("atomics", "block_reduce_latency_cyc", 5.0, "N/A", "unit N/A with value"),
