@@ -849,9 +849,11 @@ def _nccl_reference(ranks, nbytes, reps=5, warm=2) -> dict:
 def probe_p2p(args, ranks) -> dict:
     """Config: 256 MiB seeded random bytes per GPU exchanged over NVLink,
     ring (-> rank+1) and all-to-all (N chunks, each rank visiting its peers
-    in staggered order), by in-kernel peer stores, by in-kernel bulk copies
-    and by the copy engines (all peers at once, or one or two streams
-    visiting them in turn); bit-exact receive check.  Time = max over ranks
+    in staggered order), by in-kernel peer stores, by in-kernel bulk copies,
+    by the copy engines (all peers at once, or one or two streams visiting
+    them in turn) and by both at once (hybrid_<P>_<S>: the copy engines take
+    P/1000 of every job on S streams, peer stores the rest); bit-exact
+    receive check.  Time = max over ranks
     of each rank's device time (CUDA events), median of 5 repetitions.  The
     fraction of the peer-copy ceiling divides by the copy engines' ring rate
     measured in the same run; NCCL's send/recv ring and all_to_all_single on
@@ -865,9 +867,9 @@ def probe_p2p(args, ranks) -> dict:
     sh = ctypes.c_void_p(stream.cuda_stream)
     ex = multi_gpu.PeerExchange(ranks, nbytes, SEED)
     out = {}
-    methods = {"ring": ("copy_engine", "store", "bulk"),
+    methods = {"ring": ("copy_engine", "store", "bulk", "hybrid_700_1"),
                "alltoall": ("store", "bulk", "copy_engine", "copy_engine_1stream",
-                            "copy_engine_2stream")}
+                            "copy_engine_2stream", "hybrid_500_1")}
     try:
         for mode in ("ring", "alltoall"):
             egress = multi_gpu.egress_bytes(mode, ranks.rank, ranks.world, nbytes)
@@ -895,7 +897,8 @@ def probe_p2p(args, ranks) -> dict:
                     "frac_of_900_spec": round(link / 900.0, 4),
                     "ms": round(ms, 4), "egress_bytes_per_gpu": egress,
                     "sm_ctas": {"store": "2 per SM", "bulk": "32 per job (<= SMs / jobs)"}.get(
-                        method, "0 (copy engines)"),
+                        method, "2 per SM and the copy engines" if method.startswith("hybrid")
+                        else "0 (copy engines)"),
                     "bit_exact": bad == 0}
         ceiling = out["ring_copy_engine"]["per_gpu_egress_GB/s"]
         for v in out.values():

@@ -70,6 +70,7 @@ SIGNATURES = {
     "cmb_p2p_scatter_bulk_tuned": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "cmb_p2p_scatter_copy_engine": (_i, [_p, _p, _p, _i, _p]),
     "cmb_p2p_scatter_copy_engine_tuned": (_i, [_p, _p, _p, _i, _i, _p]),
+    "cmb_p2p_scatter_hybrid": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "cmb_selftest_wait_timeout": (_i, [_u64, _p, _p, _p]),
     "cmb_compare_bytes": (_i, [_p, _p, _sz, _p, _p]),
     "cmb_benchmark_global_memory": (_i, []),

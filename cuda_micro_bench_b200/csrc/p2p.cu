@@ -427,6 +427,70 @@ int scatter_copy_engine(void *const *dst, const void *const *src, const size_t *
 }  // namespace
 }  // namespace cmb
 
+namespace cmb {
+namespace {
+
+// Job j's first head_bytes(j) go by the copy engines, the rest by peer
+// stores from the SMs; the split falls on a 4 KiB boundary so both parts
+// keep the job's alignment.
+size_t hybrid_head(size_t bytes, int ce_permille) {
+  const size_t head = bytes / 1000 * static_cast<size_t>(ce_permille) +
+                      bytes % 1000 * static_cast<size_t>(ce_permille) / 1000;
+  return head / 4096 * 4096;
+}
+
+int scatter_hybrid(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                   int ce_permille, int ce_streams, cmb_stream_t stream) {
+  int rc = check_jobs("cmb_p2p_scatter_hybrid", dst, src, bytes, n);
+  if (rc) return rc;
+  if (ce_permille < 0 || ce_permille > 1000)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_hybrid: ce_permille %d not in [0, 1000]",
+                ce_permille);
+  if (ce_streams < 1 || ce_streams > kMaxJobs)
+    return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_hybrid: %d streams not in [1, 8]",
+                ce_streams);
+  void *tail_dst[kMaxJobs];
+  const void *tail_src[kMaxJobs];
+  size_t head[kMaxJobs], tail[kMaxJobs];
+  int vb = 32;
+  for (int j = 0; j < n; ++j) {
+    if ((reinterpret_cast<uintptr_t>(dst[j]) | reinterpret_cast<uintptr_t>(src[j])) & 15)
+      return fail(CMB_ERR_INVALID_ARG, "cmb_p2p_scatter_hybrid: job %d not 16-byte aligned", j);
+    head[j] = hybrid_head(bytes[j], ce_permille);
+    tail[j] = bytes[j] - head[j];
+    tail_dst[j] = static_cast<char *>(dst[j]) + head[j];
+    tail_src[j] = static_cast<const char *>(src[j]) + head[j];
+    if ((reinterpret_cast<uintptr_t>(dst[j]) | reinterpret_cast<uintptr_t>(src[j])) & 31) vb = 16;
+  }
+  CeStreams *c = ce_streams_for_current_device();
+  if (c == nullptr) return fail(CMB_ERR_CUDA, "copy-engine streams could not be created");
+  // heads: forked onto the copy-engine streams, job j on stream j % ce_streams
+  const int used = ce_streams < n ? ce_streams : n;
+  CMB_CUDA_TRY(cudaEventRecord(c->fork, stream));
+  for (int q = 0; q < used; ++q) CMB_CUDA_TRY(cudaStreamWaitEvent(c->s[q], c->fork, 0));
+  for (int j = 0; j < n; ++j)
+    if (head[j] > 0)
+      CMB_CUDA_TRY(cudaMemcpyAsync(dst[j], src[j], head[j], cudaMemcpyDefault, c->s[j % used]));
+  // tails: peer stores on `stream`, meanwhile
+  rc = scatter_store(tail_dst, tail_src, tail, n, 0, vb, stream);
+  // join the heads back into `stream` (also after a failed launch, so the
+  // internal streams are never left ahead of it)
+  for (int q = 0; q < used; ++q) {
+    CMB_CUDA_TRY(cudaEventRecord(c->join[q], c->s[q]));
+    CMB_CUDA_TRY(cudaStreamWaitEvent(stream, c->join[q], 0));
+  }
+  return rc;
+}
+
+}  // namespace
+}  // namespace cmb
+
+extern "C" int cmb_p2p_scatter_hybrid(void *const *dst, const void *const *src,
+                                      const size_t *bytes, int n, int ce_permille, int ce_streams,
+                                      cmb_stream_t stream) {
+  return scatter_hybrid(dst, src, bytes, n, ce_permille, ce_streams, stream);
+}
+
 extern "C" int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src,
                                            const size_t *bytes, int n, cmb_stream_t stream) {
   return scatter_copy_engine(dst, src, bytes, n, n, stream);

@@ -4,7 +4,7 @@ One process per GPU (torchrun).  Every rank owns a send and a receive buffer
 of `nbytes` allocated with cmb_p2p_alloc; the ranks swap CUDA IPC handles of
 their receive buffers through torch.distributed, map the peers' buffers, and
 then write straight into them with the library's peer-store kernel, its
-bulk-copy kernel or its copy-engine scatter.  torch.distributed carries only the handle exchange,
+bulk-copy kernel, its copy-engine scatter or both engines at once (hybrid).  torch.distributed carries only the handle exchange,
 barriers and the max-over-ranks timing reduction: the data path uses no
 collective library.
 
@@ -68,6 +68,18 @@ def egress_bytes(mode: str, rank: int, world: int, nbytes: int) -> int:
     return sum(j.nbytes for j in plan(mode, rank, world, nbytes) if j.dst_rank != rank)
 
 
+def parse_hybrid(method: str):
+    """"hybrid_<P>_<S>": the copy engines take P/1000 of each job on S
+    internal streams, the SMs' peer stores the rest."""
+    parts = method.split("_")
+    if len(parts) != 3 or parts[0] != "hybrid":
+        raise ValueError(method)
+    permille, streams = int(parts[1]), int(parts[2])
+    if not (0 <= permille <= 1000 and 1 <= streams <= 8):
+        raise ValueError(method)
+    return permille, streams
+
+
 class PeerExchange:
     """Send/receive buffers of this rank and the mapped receive buffers of
     all peers.  `ranks` provides rank, world, barrier() and dist."""
@@ -127,6 +139,9 @@ class PeerExchange:
             self.capi.check("cmb_p2p_scatter_copy_engine_tuned", dst, src, nb, n, 1, stream)
         elif method == "copy_engine_2stream":
             self.capi.check("cmb_p2p_scatter_copy_engine_tuned", dst, src, nb, n, 2, stream)
+        elif method.startswith("hybrid_"):
+            permille, streams = parse_hybrid(method)
+            self.capi.check("cmb_p2p_scatter_hybrid", dst, src, nb, n, permille, streams, stream)
         else:
             raise ValueError(method)
 

@@ -385,6 +385,13 @@ int cmb_p2p_scatter_copy_engine(void *const *dst, const void *const *src, const 
 int cmb_p2p_scatter_copy_engine_tuned(void *const *dst, const void *const *src,
                                       const size_t *bytes, int n, int streams,
                                       cmb_stream_t stream);
+/* The same n copies by both engines at once: the first ce_permille / 1000
+ * of each job (rounded down to 4 KiB) by the copy engines on `ce_streams`
+ * (1..8) internal streams as in cmb_p2p_scatter_copy_engine_tuned, the
+ * rest by the SMs' peer stores as in cmb_p2p_scatter_store, both forked
+ * from and joined back into `stream`.  16-byte aligned pointers. */
+int cmb_p2p_scatter_hybrid(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                           int ce_permille, int ce_streams, cmb_stream_t stream);
 
 /* --- self-test of the bounded-wait rule -------------------------------- */
 

@@ -154,3 +154,12 @@ def test_peer_that_leaves_is_detected_by_timeout():
             p.kill()
     assert res[1] == "left"
     assert res[0].startswith("error after"), res[0]
+
+
+def test_hybrid_method_names():
+    assert multi_gpu.parse_hybrid("hybrid_500_1") == (500, 1)
+    assert multi_gpu.parse_hybrid("hybrid_0_8") == (0, 8)
+    assert multi_gpu.parse_hybrid("hybrid_1000_2") == (1000, 2)
+    for bad in ("hybrid_1001_1", "hybrid_500_0", "hybrid_500_9", "hybrid_500", "store_1_1"):
+        with pytest.raises(ValueError):
+            multi_gpu.parse_hybrid(bad)

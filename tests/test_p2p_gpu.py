@@ -52,6 +52,33 @@ def test_scatter_local_bit_exact(cuda, cmb, method, sizes):
     _check_jobs(cuda, src, dst, sizes)
 
 
+@pytest.mark.parametrize("permille,streams", [(0, 1), (1, 1), (500, 1), (700, 2), (999, 3),
+                                              (1000, 1)])
+@pytest.mark.parametrize("sizes", [[1 << 20], [4096 + 48, 7 << 16, 16], [5 << 20] * 8,
+                                   [(32 << 10) * 149 + 13, 0, 15, 1 << 16]])
+def test_scatter_hybrid_local_bit_exact(cuda, cmb, permille, streams, sizes):
+    """Copy-engine heads and peer-store tails of every job meet exactly,
+    from all-peer-stores (0) to all-copy-engine (1000), on ragged sizes."""
+    n = len(sizes)
+    src, dst, d, s_, nb = _local_jobs(cuda, sizes)
+    cmb.check("cmb_p2p_scatter_hybrid", d, s_, nb, n, permille, streams, stream_handle(cuda))
+    cuda.cuda.synchronize()
+    _check_jobs(cuda, src, dst, sizes)
+
+
+def test_scatter_hybrid_rejects_bad_args(cuda, cmb):
+    t = cuda.zeros(1 << 16, dtype=cuda.uint8, device="cuda")
+    one = lambda off: (ctypes.c_void_p * 1)(t.data_ptr() + off)
+    nb = (ctypes.c_size_t * 1)(4096)
+    s = stream_handle(cuda)
+    assert cmb.lib.cmb_p2p_scatter_hybrid(one(0), one(4096), nb, 1, 1001, 1, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_hybrid(one(0), one(4096), nb, 1, -1, 1, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_hybrid(one(0), one(4096), nb, 1, 500, 0, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_hybrid(one(0), one(4096), nb, 1, 500, 9, s) == 1
+    assert cmb.lib.cmb_p2p_scatter_hybrid(one(8), one(0), nb, 1, 500, 1, s) == 1  # alignment
+    assert cmb.lib.cmb_p2p_scatter_hybrid(one(0), one(4096), nb, 9, 500, 1, s) == 1  # > 8 jobs
+
+
 @pytest.mark.parametrize("chunk,stages,ctas", [(16, 4, 3), (4096, 8, 0), (56 << 10, 4, 1),
                                                (16 << 10, 8, 200), (32 << 10, 4, 0)])
 def test_scatter_bulk_shapes(cuda, cmb, chunk, stages, ctas):
@@ -102,7 +129,8 @@ def _free_port():
     return port
 
 
-ALL_METHODS = ("store", "bulk", "copy_engine", "copy_engine_1stream", "copy_engine_2stream")
+ALL_METHODS = ("store", "bulk", "copy_engine", "copy_engine_1stream", "copy_engine_2stream",
+               "hybrid_500_1", "hybrid_300_2")
 
 
 def _rank(rank, world, port, q, device=None, backend="nccl"):
