@@ -11,7 +11,8 @@
 // CTA that runs on the SM under test time dependent loads of kLines lines of
 // a separate, never-written region (every other CTA of the launch only
 // stays resident long enough that each SM holds exactly one CTA).  The host
-// splits the SMs by their pattern and checks that the split is clean.  The
+// splits the SMs by their pattern and checks that the split is clean (a
+// pass that is not is measured once more before it fails).  The
 // map feeds the GEMM's die-split tile order (cmb_gemm_set_sm_die_map); it
 // differs between B200s (which SMs are fused off varies per part), so it is
 // measured on the device that uses it.
@@ -152,62 +153,69 @@ extern "C" int cmb_sm_die_map(uint8_t *sm_die, int capacity, int *n_ids, float *
     return fail(CMB_ERR_INVALID_ARG, "cmb_sm_die_map: capacity %d below %d SM ids", capacity,
                 id_end);
 
-  for (int rep = 0; rep < kReps; ++rep) {
-    for (int t : ids) {
-      CMB_CUDA_TRY(cudaMemsetAsync(flush, (rep * 31 + t) & 0xFF, kFlushBytes, stream));
-      k_die_probe<<<nsm, 32, kProbeSmem, stream>>>(region, lines_d, t,
-                                                   lat_d + static_cast<size_t>(t) * kLines,
-                                                   found_d + t);
-      CMB_LAUNCH_CHECK();
-    }
-  }
-  std::vector<int> found(CMB_DIE_MAP_IDS);
-  std::vector<uint32_t> lat(static_cast<size_t>(CMB_DIE_MAP_IDS) * kLines);
-  CMB_CUDA_TRY(cudaMemcpyAsync(found.data(), found_d, found.size() * sizeof(int),
-                               cudaMemcpyDeviceToHost, stream));
-  CMB_CUDA_TRY(cudaMemcpyAsync(lat.data(), lat_d, lat.size() * sizeof(uint32_t),
-                               cudaMemcpyDeviceToHost, stream));
-  CMB_CUDA_TRY(cudaStreamSynchronize(stream));
-  for (int t : ids)
-    if (found[t] != kReps)
-      return fail(CMB_ERR_MISMATCH, "cmb_sm_die_map: SM %d ran the probe %d times, not %d", t,
-                  found[t], kReps);
-
-  // per line: far (1) when slower than the median over SMs
+  // Measure and split; a split that is not clean (a noisy pass) is measured
+  // once more before it is reported.
   const size_t n = ids.size();
-  std::vector<std::vector<uint8_t>> far(n, std::vector<uint8_t>(kLines));
-  std::vector<double> near_lat, far_lat;
-  for (int j = 0; j < kLines; ++j) {
-    std::vector<double> col(n);
-    for (size_t i = 0; i < n; ++i) col[i] = lat[static_cast<size_t>(ids[i]) * kLines + j];
-    const double m = median(col);
-    for (size_t i = 0; i < n; ++i) {
-      far[i][j] = col[i] > m ? 1 : 0;
-      (far[i][j] ? far_lat : near_lat).push_back(col[i]);
-    }
-  }
-  // die 0 = the SMs whose pattern agrees with the lowest SM id's
   std::vector<uint8_t> die(n);
-  int count[2] = {0, 0};
-  double worst = 0.0;
-  for (size_t i = 0; i < n; ++i) {
-    int same = 0;
-    for (int j = 0; j < kLines; ++j) same += far[i][j] == far[0][j];
-    const double agree = static_cast<double>(same) / kLines;
-    die[i] = agree > 0.5 ? 0 : 1;
-    ++count[die[i]];
-    worst = std::max(worst, std::min(agree, 1.0 - agree));
+  for (int attempt = 0;; ++attempt) {
+    CMB_CUDA_TRY(cudaMemsetAsync(found_d, 0, CMB_DIE_MAP_IDS * sizeof(int), stream));
+    for (int rep = 0; rep < kReps; ++rep) {
+      for (int t : ids) {
+        CMB_CUDA_TRY(cudaMemsetAsync(flush, (attempt * 61 + rep * 31 + t) & 0xFF, kFlushBytes,
+                                     stream));
+        k_die_probe<<<nsm, 32, kProbeSmem, stream>>>(region, lines_d, t,
+                                                     lat_d + static_cast<size_t>(t) * kLines,
+                                                     found_d + t);
+        CMB_LAUNCH_CHECK();
+      }
+    }
+    std::vector<int> found(CMB_DIE_MAP_IDS);
+    std::vector<uint32_t> lat(static_cast<size_t>(CMB_DIE_MAP_IDS) * kLines);
+    CMB_CUDA_TRY(cudaMemcpyAsync(found.data(), found_d, found.size() * sizeof(int),
+                                 cudaMemcpyDeviceToHost, stream));
+    CMB_CUDA_TRY(cudaMemcpyAsync(lat.data(), lat_d, lat.size() * sizeof(uint32_t),
+                                 cudaMemcpyDeviceToHost, stream));
+    CMB_CUDA_TRY(cudaStreamSynchronize(stream));
+    for (int t : ids)
+      if (found[t] != kReps)
+        return fail(CMB_ERR_MISMATCH, "cmb_sm_die_map: SM %d ran the probe %d times, not %d", t,
+                    found[t], kReps);
+
+    // per line: far (1) when slower than the median over SMs
+    std::vector<std::vector<uint8_t>> far(n, std::vector<uint8_t>(kLines));
+    std::vector<double> near_lat, far_lat;
+    for (int j = 0; j < kLines; ++j) {
+      std::vector<double> col(n);
+      for (size_t i = 0; i < n; ++i) col[i] = lat[static_cast<size_t>(ids[i]) * kLines + j];
+      const double m = median(col);
+      for (size_t i = 0; i < n; ++i) {
+        far[i][j] = col[i] > m ? 1 : 0;
+        (far[i][j] ? far_lat : near_lat).push_back(col[i]);
+      }
+    }
+    // die 0 = the SMs whose pattern agrees with the lowest SM id's
+    int count[2] = {0, 0};
+    double worst = 0.0;
+    for (size_t i = 0; i < n; ++i) {
+      int same = 0;
+      for (int j = 0; j < kLines; ++j) same += far[i][j] == far[0][j];
+      const double agree = static_cast<double>(same) / kLines;
+      die[i] = agree > 0.5 ? 0 : 1;
+      ++count[die[i]];
+      worst = std::max(worst, std::min(agree, 1.0 - agree));
+    }
+    const double near_med = median(near_lat), far_med = median(far_lat);
+    if (near_far_cycles != nullptr) {
+      near_far_cycles[0] = static_cast<float>(near_med);
+      near_far_cycles[1] = static_cast<float>(far_med);
+    }
+    if (count[0] > 0 && count[1] > 0 && worst <= 0.35 && far_med - near_med >= 100.0) break;
+    if (attempt == 1)
+      return fail(CMB_ERR_MISMATCH,
+                  "cmb_sm_die_map: no clean two-die split (%d / %d SMs, worst pattern agreement "
+                  "%.2f, near %.0f / far %.0f cycles)",
+                  count[0], count[1], 1.0 - worst, near_med, far_med);
   }
-  const double near_med = median(near_lat), far_med = median(far_lat);
-  if (near_far_cycles != nullptr) {
-    near_far_cycles[0] = static_cast<float>(near_med);
-    near_far_cycles[1] = static_cast<float>(far_med);
-  }
-  if (count[0] == 0 || count[1] == 0 || worst > 0.35 || far_med - near_med < 100.0)
-    return fail(CMB_ERR_MISMATCH,
-                "cmb_sm_die_map: no clean two-die split (%d / %d SMs, worst pattern agreement "
-                "%.2f, near %.0f / far %.0f cycles)",
-                count[0], count[1], 1.0 - worst, near_med, far_med);
   for (int i = 0; i < capacity; ++i) sm_die[i] = 0xFF;
   for (size_t i = 0; i < n; ++i) sm_die[ids[i]] = die[i];
   *n_ids = id_end;

@@ -287,7 +287,7 @@ int cmb_quantize_e4m3(const uint16_t *src_bf16, size_t n, uint8_t *dst, float *s
  * short launches on `stream` (tens of ms), allocates and frees 288 MiB of
  * device memory, and needs the device otherwise idle (every SM must take
  * one of its CTAs).  CMB_ERR_MISMATCH when the SMs do not split cleanly in
- * two. */
+ * two (after a second measurement). */
 int cmb_sm_die_map(uint8_t *sm_die, int capacity, int *n_ids, float *near_far_cycles,
                    cmb_stream_t stream);
 /* Installs a die map (as cmb_sm_die_map returns it: n_ids entries of 0, 1
