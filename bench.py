@@ -984,6 +984,48 @@ def probe_gemm_die(torch, stream, sh) -> dict:
     return out
 
 
+def probe_copy_forms(torch, stream, sh) -> dict:
+    """The 4 GiB device copy by every engine this library drives, for
+    placing the copy stream against the device's own copy ceiling: the
+    load/store-unit stream (cmb_stream_copy), the peer-store kernel on one
+    local job, bulk copies through shared memory (the P2P bulk kernel on one
+    local job, several chunk / ring / CTA shapes) and the copy engines
+    (cudaMemcpyAsync device to device through torch).  GB/s = 2 x 4 GiB /
+    median of 12 launches after 3 warm-up launches; every output compared
+    with the source bit for bit."""
+    from cuda_micro_bench_b200 import check
+
+    n = 1 << 30
+    nbytes = 4 * n
+    src = torch.empty(n, dtype=torch.float32, device="cuda")
+    dst = torch.empty(n, dtype=torch.float32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    check("cmb_fill_uniform_f32", ctypes.c_void_p(src.data_ptr()), n, ctypes.c_uint64(SEED), sh)
+    D = (ctypes.c_void_p * 1)(dst.data_ptr())
+    S = (ctypes.c_void_p * 1)(src.data_ptr())
+    NB = (ctypes.c_size_t * 1)(nbytes)
+    forms = {
+        "stream_copy": lambda: check("cmb_stream_copy", ctypes.c_void_p(dst.data_ptr()),
+                                     ctypes.c_void_p(src.data_ptr()), nbytes, sh),
+        "peer_store_kernel_local": lambda: check("cmb_p2p_scatter_store", D, S, NB, 1, 0, sh),
+        "copy_engine_d2d": lambda: dst.copy_(src),
+    }
+    for chunk, stages, ctas in ((16384, 4, 148), (16384, 8, 148), (32768, 4, 148),
+                                (8192, 4, 444)):
+        forms[f"bulk_{chunk // 1024}k_{stages}stages_{ctas}ctas"] = (
+            lambda chunk=chunk, stages=stages, ctas=ctas: check(
+                "cmb_p2p_scatter_bulk_tuned", D, S, NB, 1, ctas, chunk, stages,
+                ctypes.c_void_p(status.data_ptr()), sh))
+    out = {}
+    for name, fn in forms.items():
+        dst.zero_()
+        ms = _median_ms(torch, stream, fn, reps=12, warm=3)
+        out[name] = {"GB/s": round(2 * nbytes / (ms * 1e-3) / 1e9, 1),
+                     "bit_exact": bool(torch.equal(dst, src)), "status": int(status.item())}
+    del src, dst
+    return out
+
+
 def run_probe_only(args) -> int:
     """Runs only the named probes (for profiling) and prints their results."""
     import torch
@@ -1008,6 +1050,8 @@ def run_probe_only(args) -> int:
             out["gemm_256x256"] = probe_cublas(torch, stream, sh, ours_tile256=True)
         elif name == "gemm_die":
             out["gemm_die"] = probe_gemm_die(torch, stream, sh)
+        elif name == "copy_forms":
+            out["copy_forms_4gib"] = probe_copy_forms(torch, stream, sh)
         torch.cuda.empty_cache()
     print(json.dumps({"probes": out}), flush=True)
     return 0
@@ -1118,7 +1162,8 @@ def main(argv=None) -> int:
     ap.add_argument("--quick-chase", action="store_true",
                     help="2^22 chase hops instead of the configuration's 2^24")
     ap.add_argument("--probe", action="append",
-                    choices=["stream", "chase", "tma", "gemm", "cublas", "gemm256", "gemm_die"],
+                    choices=["stream", "chase", "tma", "gemm", "cublas", "gemm256", "gemm_die",
+                             "copy_forms"],
                     help="run only this probe (repeatable); no headline line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
