@@ -5,10 +5,10 @@ the load/store units against TMA (results/report.html:550-559,
 TMA_LSU_COMPARE: memory_dram.read_bw_gibps against
 tma.tma_g2s_load_bw_gibps).  This module renders that row and the rows the
 B200 probes add beside it: the copy stream against the TMA tile copy, the
-legacy mma.sync issue rate against the tcgen05 GEMM (bf16 and e4m3), and the
-NVLink ring and all-to-all by peer stores, bulk copies and copy engines.
-Each row names the two keys it reads; a key the run did not log shows as
-"n/a".
+legacy mma.sync issue rate against the tcgen05 GEMM (bf16 and e4m3; in the
+plain and the die-split tile order, and with bf16 C), and the NVLink ring and
+all-to-all by peer stores, bulk copies and copy engines.  Each row names the
+keys it reads; a key the run did not log shows as "n/a".
 
     python -m cuda_micro_bench_b200.compare [results/results.json]
 """
@@ -30,14 +30,18 @@ ROWS = [
     ("BF16 tensor throughput", "TFLOP/s", [
         ("mma.sync m16n8k16 issue rate (registers only)", "tensor_core_extended",
          "bf16_m16n8k16_throughput_TFs", 1.0),
-        ("tcgen05 GEMM 8192^3 (TMA, TMEM, checked)", "tensor_core_tcgen05",
+        ("tcgen05 GEMM 8192^3, plain tile order", "tensor_core_tcgen05",
+         "bf16_gemm_8192_plain_order_tflops", 1.0),
+        ("tcgen05 GEMM 8192^3 (TMA, TMEM, checked; die-split order)", "tensor_core_tcgen05",
          "bf16_gemm_8192_tflops", 1.0),
         ("tcgen05 GEMM 8192^3, bf16 C", "tensor_core_tcgen05", "bf16_gemm_8192_bf16out_tflops",
          1.0)]),
     ("FP8 e4m3 tensor throughput", "TFLOP/s", [
         ("mma.sync m16n8k32 issue rate (registers only)", "tensor_core_extended",
          "fp8_m16n8k32_throughput_TFs", 1.0),
-        ("tcgen05 GEMM 8192^3 (TMA, TMEM, checked)", "tensor_core_tcgen05",
+        ("tcgen05 GEMM 8192^3, plain tile order", "tensor_core_tcgen05",
+         "fp8_e4m3_gemm_8192_plain_order_tflops", 1.0),
+        ("tcgen05 GEMM 8192^3 (TMA, TMEM, checked; die-split order)", "tensor_core_tcgen05",
          "fp8_e4m3_gemm_8192_tflops", 1.0),
         ("tcgen05 GEMM 8192^3, bf16 C", "tensor_core_tcgen05",
          "fp8_e4m3_gemm_8192_bf16out_tflops", 1.0)]),

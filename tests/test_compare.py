@@ -25,7 +25,7 @@ def test_rows_read_the_reports_keys_and_mark_the_best():
     assert best == "copy engines"
     # rows whose keys the run did not log
     vals, best = rows["BF16 tensor throughput"]
-    assert [v for _, v in vals] == [None, None, None] and best is None
+    assert [v for _, v in vals] == [None, None, None, None] and best is None
 
 
 def test_markdown_and_cli(tmp_path, capsys):
@@ -36,6 +36,7 @@ def test_markdown_and_cli(tmp_path, capsys):
     md = compare.markdown(doc)
     assert "| DRAM copy bandwidth (read + write) | LSU copy stream (best) | 6,500.0 GB/s |  |" in md
     assert "3.11x" in md  # 1519 / 488
+    assert "die-split order" in md and "plain tile order" in md
     assert "n/a" in md
     path = tmp_path / "r.json"
     path.write_text(json.dumps(doc))
