@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -122,6 +123,53 @@ double host_uniform_sum(size_t n, uint64_t seed) {
   return s;
 }
 
+double seconds_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// The host side of the stream probes, on the same data: the fp32 values the
+// device summed and copied, summed in fp64 and copied by every host thread
+// (contiguous block per thread).  `sum` must equal the fp64 reference sum of
+// the seeded stream (same values, same order per block).
+struct HostStream {
+  double sum, sum_gbps, memcpy_gbps;
+};
+
+HostStream host_stream(const std::vector<float> &x) {
+  const unsigned nt = host_threads();
+  const size_t n = x.size();
+  std::vector<float> y(n);
+  std::vector<double> part(nt, 0.0);
+  HostStream r{};
+  {
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<std::thread> pool;
+    for (unsigned t = 0; t < nt; ++t)
+      pool.emplace_back([&, t] {
+        double s = 0.0;
+        for (size_t i = n * t / nt; i < n * (t + 1) / nt; ++i) s += static_cast<double>(x[i]);
+        part[t] = s;
+      });
+    for (auto &th : pool) th.join();
+    r.sum_gbps = 4.0 * n / seconds_since(t0) / 1e9;
+  }
+  r.sum = 0.0;
+  for (double v : part) r.sum += v;
+  {
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<std::thread> pool;
+    for (unsigned t = 0; t < nt; ++t)
+      pool.emplace_back([&, t] {
+        const size_t a = n * t / nt, b = n * (t + 1) / nt;
+        std::memcpy(y.data() + a, x.data() + a, (b - a) * sizeof(float));
+      });
+    for (auto &th : pool) th.join();
+    r.memcpy_gbps = 2.0 * 4.0 * n / seconds_since(t0) / 1e9;
+  }
+  if (std::memcmp(x.data(), y.data(), n * sizeof(float)) != 0) r.memcpy_gbps = -1.0;
+  return r;
+}
+
 int expect_equal(const void *a, const void *b, size_t bytes, bool *equal) {
   DevBuf cnt;
   TRY(cnt.alloc(sizeof(unsigned long long)));
@@ -136,6 +184,7 @@ int expect_equal(const void *a, const void *b, size_t bytes, bool *equal) {
 
 struct ChaseResult {
   double cycles_per_hop, ns_per_hop;
+  double host_ns_per_hop;  // the host walk of the same cycle (one thread)
 };
 
 // Dependent-load chase over `bytes` (include/memory_chase.h:11-59): the link
@@ -151,7 +200,9 @@ int measure_chase(size_t bytes, bool bypass_l1, bool resident, ChaseResult *res)
   const uint64_t warmup = resident ? 2 * slots : 1024;
   const uint64_t hops = resident ? (1u << 17) : (1u << 24);
   uint32_t expect = 0;
+  const auto walk0 = std::chrono::steady_clock::now();
   TRY(cmb_chase_host_walk(links.data(), words, warmup + hops, &expect));
+  res->host_ns_per_hop = seconds_since(walk0) * 1e9 / static_cast<double>(warmup + hops);
   DevBuf d, out;
   TRY(d.alloc(bytes));
   TRY(out.alloc(4 * sizeof(uint64_t)));
@@ -343,6 +394,19 @@ int section_global_memory() {
     CMB_CUDA_TRY(cudaMemcpy(&got, sum.p, sizeof(got), cudaMemcpyDeviceToHost));
     const double ref = host_uniform_sum(n, kStreamSeed);
     rel_err = std::fabs(got - ref) / std::max(std::fabs(ref), 1e-300);
+    if (bytes == sizes[3]) {  // the host reference on the same 1 GiB
+      std::vector<float> hx(n);
+      CMB_CUDA_TRY(cudaMemcpy(hx.data(), a.p, bytes, cudaMemcpyDeviceToHost));
+      const HostStream hs = host_stream(hx);
+      if (hs.memcpy_gbps < 0) return fail(CMB_ERR_MISMATCH, "host reference memcpy differs");
+      if (hs.sum != ref)
+        return fail(CMB_ERR_MISMATCH, "host sum of the device stream %.17g != %.17g", hs.sum, ref);
+      printf("  host reference (%u threads, 1 GiB): fp64 sum %.1f GB/s, memcpy %.1f GB/s "
+             "(read+write)\n", host_threads(), hs.sum_gbps, hs.memcpy_gbps);
+      g_results.log("host_ref", "cores", host_threads(), "threads");
+      g_results.log("host_ref", "sum_gbps", hs.sum_gbps, "GB/s");
+      g_results.log("host_ref", "memcpy_gbps", hs.memcpy_gbps, "GB/s");
+    }
     copy_gib = gib_per_s(2.0 * bytes, cms);
     read_gib = gib_per_s((double)bytes, rms);
     copy_gbs = gb_per_s(2.0 * bytes, cms);
@@ -362,6 +426,7 @@ int section_global_memory() {
   g_results.log("memory_dram", "read_frac_of_8tbs_spec", read_gbs / 8000.0, "");
   g_results.log("memory_dram", "copy_verified", copy_ok ? 1.0 : 0.0, "bool");
   g_results.log("memory_dram", "read_sum_rel_err", rel_err, "");
+  g_results.log("memory_dram", "stream_seed", static_cast<double>(kStreamSeed), "seed");
 
   // DRAM latency: 512 MiB link array (well above the 126 MB L2), .cg loads.
   const size_t bytes = std::min<size_t>(512ull << 20, info.total_global_mem / 8);
@@ -377,6 +442,9 @@ int section_global_memory() {
   g_results.log("memory_dram", "chase_loads_per_sample", (double)(1u << 24), "loads");
   g_results.log("memory_dram", "chase_min_sector_footprint_bytes", (double)(bytes / 4), "bytes");
   g_results.log("memory_dram", "chase_endpoint_verified", 1.0, "bool");
+  g_results.log("memory_dram", "chase_seed", static_cast<double>(kChaseSeed), "seed");
+  printf("  host walk of the same cycle (one thread): %.2f ns per hop\n", cr.host_ns_per_hop);
+  g_results.log("host_ref", "chase_ns_per_hop", cr.host_ns_per_hop, "ns");
   return CMB_OK;
 }
 
@@ -608,6 +676,7 @@ int section_tma() {
   g_results.log("tma", "tile_copy_bw_gbps", gb_per_s(2.0 * bytes, cms), "GB/s");
   g_results.log("tma", "tile_copy_frac_of_8tbs_spec", gb_per_s(2.0 * bytes, cms) / 8000.0, "");
   g_results.log("tma", "tile_copy_verified", 1.0, "bool");
+  g_results.log("tma", "tile_seed", static_cast<double>(kStreamSeed), "seed");
   g_results.log("tma", "tile_box_rows", 128, "");
   g_results.log("tma", "tile_box_cols", 128, "");
   g_results.log("tma", "tile_stages", 4, "");
@@ -776,8 +845,13 @@ int section_tensor_core_extended() {
       CMB_CUDA_TRY(cudaMemcpy(hs2, sb.p, sizeof(hs2), cudaMemcpyDeviceToHost));
     }
     // 64 sampled 256 x 256 output tiles against fp64 products
+    const auto check0 = std::chrono::steady_clock::now();
     const double err = fp8 ? sampled_gemm_error<true>(ha, hb, hc, M, N, K, hs[0], hs2[0], 64)
                            : sampled_gemm_error<false>(ha, hb, hc, M, N, K, 1.0, 1.0, 64);
+    if (!fp8) {  // the host reference's rate: fp64 products of those tiles, every host thread
+      const double host_tf = 64.0 * 2.0 * 256 * 256 * K / seconds_since(check0) / 1e12;
+      g_results.log("host_ref", "gemm_fp64_tiles_tflops", host_tf, "TFLOP/s");
+    }
     const double tf = flop / (ms * 1e-3) / 1e12;
     const double spec = fp8 ? 4500.0 : 2250.0;
     const std::string p = fp8 ? "fp8_e4m3_gemm_8192" : "bf16_gemm_8192";
@@ -785,6 +859,7 @@ int section_tensor_core_extended() {
            "rel err %.1e\n", fp8 ? "e4m3" : "bf16", tf, 100 * tf / spec, spec, err);
     if (err > 1e-2) return fail(CMB_ERR_MISMATCH, "%s: sampled rel err %.3g > 1e-2", p.c_str(), err);
     g_results.log("tensor_core_tcgen05", p + "_tflops", tf, "TFLOP/s");
+    g_results.log("tensor_core_tcgen05", "gemm_seed", static_cast<double>(kGemmSeed), "seed");
     if (die_rc == CMB_OK) {
       const double tfp = flop / (ms_plain * 1e-3) / 1e12;
       printf("  (plain tile order: %.1f TFLOP/s)\n", tfp);
@@ -1010,6 +1085,7 @@ int multi_gpu_body(std::vector<GpuSide> &g, size_t bytes) {
   printf("  sharded copy stream, %d GPUs: %.1f GB/s aggregate\n", n, agg);
   g_results.log("p2p", "sharded_stream_aggregate_gbps", agg, "GB/s");
   g_results.log("p2p", "gpus_used", n, "");
+  g_results.log("p2p", "seed", static_cast<double>(kStreamSeed), "seed");
   return CMB_OK;
 }
 

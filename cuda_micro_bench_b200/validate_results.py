@@ -158,6 +158,10 @@ def check(doc, full=True, keys=None):
         if err is not None and err > 1e-2:
             fail(f"tensor_core_tcgen05.{p}_max_rel_err = {err} above 1e-2")
     bound("peak", "fp16_tensor_tflops", 0, B200["bf16_tflops"] * 1.05, "dense fp16 tensor peak")
+    # the host reference beside the GPU probes
+    bound("host_ref", "cores", 0, 1024, "host threads")
+    for k in ("sum_gbps", "memcpy_gbps", "chase_ns_per_hop", "gemm_fp64_tiles_tflops"):
+        bound("host_ref", k, 0, 1e6, "a positive host timing")
     # the die map: every SM on one of two dies, far loads slower than near
     dies = [val("tensor_core_tcgen05", f"sms_on_die{d}") for d in (0, 1)]
     if all(x is not None for x in dies) and (min(dies) <= 0 or sum(dies) != B200["sm_count"]):

@@ -59,6 +59,14 @@ def test_cli_full_run(cuda, tmp_path):
     assert v("memory_more", "l2_aggregate_verified") == 1.0
     assert v("memory_more", "l2_aggregate_bw_gbps") > v("memory", "dram_read_bw_gbps")
     assert 5 < v("pcie", "htod_bandwidth_GiB_s") < 128 and 5 < v("pcie", "dtoh_bandwidth_GiB_s") < 128
+    # the host reference on the same data, and the seeds of the synthetic inputs
+    assert v("host_ref", "cores") >= 1
+    assert v("host_ref", "sum_gbps") > 0 and v("host_ref", "memcpy_gbps") > 0
+    assert v("host_ref", "chase_ns_per_hop") > 1 and v("host_ref", "gemm_fp64_tiles_tflops") > 0
+    assert v("memory_dram", "stream_seed") == 0x5EED and v("memory_dram", "chase_seed") == 0xC0DA
+    assert v("tensor_core_tcgen05", "gemm_seed") == 0x6E33 and v("tma", "tile_seed") == 0x5EED
+    # the die map the GEMMs ran with
+    assert v("tensor_core_tcgen05", "sms_on_die0") + v("tensor_core_tcgen05", "sms_on_die1") == 148
     from cuda_micro_bench_b200 import compare, validate_results
     assert validate_results.check(doc) == []
     table = compare.markdown(doc)

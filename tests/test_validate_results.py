@@ -57,6 +57,13 @@ MEASURED = [
     ("tensor_core_tcgen05", "bf16_gemm_8192_tflops", 1519.0, "TFLOP/s"),
     ("tensor_core_tcgen05", "bf16_gemm_8192_plain_order_tflops", 1501.0, "TFLOP/s"),
     ("tensor_core_tcgen05", "sms_on_die0", 70.0, "count"),
+    ("tensor_core_tcgen05", "gemm_seed", 28211.0, "seed"),
+    ("memory_dram", "stream_seed", 24301.0, "seed"),
+    ("host_ref", "cores", 16.0, "threads"),
+    ("host_ref", "sum_gbps", 80.0, "GB/s"),
+    ("host_ref", "memcpy_gbps", 120.0, "GB/s"),
+    ("host_ref", "chase_ns_per_hop", 100.0, "ns"),
+    ("host_ref", "gemm_fp64_tiles_tflops", 0.05, "TFLOP/s"),
     ("tensor_core_tcgen05", "sms_on_die1", 78.0, "count"),
     ("tensor_core_tcgen05", "die_near_load_latency_cyc", 610.0, "cycles"),
     ("tensor_core_tcgen05", "die_far_load_latency_cyc", 1000.0, "cycles"),
@@ -118,6 +125,7 @@ def _set(doc, sec, key, value, unit=None):
     ("tensor_core_tcgen05", "bf16_gemm_8192_plain_order_tflops", 2600.0, None, "dense tensor peak"),
     ("tensor_core_tcgen05", "sms_on_die1", 70.0, None, "not a split of"),
     ("tensor_core_tcgen05", "die_far_load_latency_cyc", 500.0, None, "die load latency"),
+    ("host_ref", "cores", 0.0, None, "host threads"),
     ("p2p", "ring_store_link_gbps", 1000.0, None, "NVLink 5"),
     ("pcie", "htod_bandwidth_GiB_s", 80.0, None, "PCIe Gen5"),
     ("atomics", "block_reduce_latency_cyc", 5.0, "N/A", "unit N/A with value"),
