@@ -9,8 +9,9 @@
 //
 // The probe, once per SM: evict L2 by writing a 256 MiB buffer, then let the
 // CTA that runs on the SM under test time dependent loads of kLines lines of
-// a separate, never-written region (every other CTA of the launch only
-// stays resident long enough that each SM holds exactly one CTA).  The host
+// a separate region, zeroed once before the first pass and not written by it
+// (every other CTA of the launch only stays resident long enough that each
+// SM holds exactly one CTA).  The host
 // splits the SMs by their pattern and checks that the split is clean (a
 // pass that is not is measured once more before it fails).  The
 // map feeds the GEMM's die-split tile order (cmb_gemm_set_sm_die_map); it
